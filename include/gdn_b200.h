@@ -1,0 +1,135 @@
+/*
+ * gdn_b200: B200 (sm_100a) kernels for the Qwen3.8 / Qwen3-Next gated delta
+ * net (GDN) layer hot path, behind a plain C ABI.
+ *
+ * Every entry point takes device pointers, sizes and a cudaStream_t passed as
+ * void*, enqueues its kernels on that stream and returns without waiting.
+ * Nothing here allocates device memory: scratch space is passed in by the
+ * caller (query its size with the matching *_workspace_bytes function).
+ * Return values are the STATECENTRIC_QWEN38_* status codes of
+ * statecentric_qwen38_provider_api_v1.h; gdn_b200_last_error() returns the
+ * message of the last failure on the calling thread.
+ *
+ * Citations name the reference operator each entry point replaces
+ * (P = native/src/qwen38_geometry_normalized_gdn_provider.cpp).
+ *
+ * Tensor layouts (row-major, contiguous):
+ *   q, k        bf16 [T, Hk, 128]   raw (not yet L2-normalised)
+ *   v, z, o     bf16 [T, Hv, 128]
+ *   a, b        bf16 [T, Hv]        gate inputs: g = -exp(A_log)*softplus(a+dt_bias),
+ *                                   beta = sigmoid(b)
+ *   A_log, dt_bias  f32 [Hv]
+ *   gamma       bf16 [128]          output RMSNorm weight (eps 1e-6)
+ *   w_out       bf16 [hidden, Hv*128]  (reference input 9: dims {value, hidden},
+ *                                   strides {1, value}, P:2405-2406)
+ *   state       f32 [S, Hv, 128(v), 128(k)]  recurrent state, row = value
+ *                                   index, contiguous along key; updated in place
+ *   out         bf16 [T, hidden]    rank-partial when heads are sharded
+ *   cu_seqlens  int32 host array [S+1], packed prefix sums of sequence lengths
+ * Sequence s owns tokens [cu_seqlens[s], cu_seqlens[s+1]) and state row s.
+ * v-head h reads q/k head h / (Hv / Hk).
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stdint.h>
+
+#include "statecentric_qwen38_provider_api_v1.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define GDN_B200_API __attribute__((visibility("default")))
+#else
+#define GDN_B200_API
+#endif
+
+#define GDN_B200_HEAD_DIM 128
+#define GDN_B200_CHUNK 64
+#define GDN_B200_MAX_SEQUENCES 1024
+
+/* Message of the last failed call on this thread ("" when none). */
+GDN_B200_API const char* gdn_b200_last_error(void);
+
+/* Every entry point that takes a workspace keeps a device error word in its
+ * first 256 bytes.  Kernels never spin without a time limit: a wait that runs
+ * out records an error there and the kernel exits.  This call synchronises
+ * `stream` and returns OK, or INTERNAL with the reason. */
+GDN_B200_API int32_t gdn_b200_workspace_status(const void* workspace, void* stream);
+
+/* Output tail: out = bf16( bf16(bf16(RMSNorm_head(o)*gamma) * bf16(SiLU(z))) @ w_out^T ).
+ * Replaces BatchGdnOutputTail (P:1434-1498; flattened matmul since
+ * patches/0001-feat-qwen38-flatten-dual-tail-output-projection.patch:179-184),
+ * LaneGdnOutputTailV13 (P:1371-1432) and the single-sequence tail (P:3498-3547):
+ * rows = B*T of every sequence, flattened into one GEMM. */
+GDN_B200_API uint64_t gdn_b200_output_tail_workspace_bytes(int64_t rows, int32_t value_heads,
+                                              int32_t hidden);
+GDN_B200_API int32_t gdn_b200_output_tail(const void* o, const void* z, const void* gamma,
+                             const void* w_out, void* out, int64_t rows,
+                             int32_t value_heads, int32_t hidden, float eps,
+                             void* workspace, uint64_t workspace_bytes,
+                             void* stream);
+
+/* One decode step for `batch` sequences of one token each: gating, q/k
+ * L2-norm, S <- exp(g) S; S += beta k (v - S^T k)^T; o = scale S^T q,
+ * scale = 128^-1/2.  Replaces PackedDecodeRecurrentV12 (P:1308-1369) with the
+ * gating (P:3310-3339) and q/k RmsNorm (P:3249-3308) fused in.  o_out may be
+ * NULL.  When z and gated_out are not NULL the tail prologue
+ * bf16(bf16(RMSNorm(o)*gamma)*bf16(SiLU(z))) is fused too and written to
+ * gated_out [batch, Hv*128]. */
+GDN_B200_API int32_t gdn_b200_decode_step(const void* q, const void* k, const void* v,
+                             const void* a, const void* b, const float* A_log,
+                             const float* dt_bias, float* state, void* o_out,
+                             const void* z, const void* gamma, void* gated_out,
+                             int32_t batch, int32_t qk_heads,
+                             int32_t value_heads, void* stream);
+
+/* Chunked (C = 64) gated delta rule over packed variable-length sequences.
+ * Replaces ChunkGdn (P:1641-1838) and the token-serial run_sequence
+ * (P:3387-3469): every sequence length, any number of chunks, one call. */
+GDN_B200_API uint64_t gdn_b200_chunk_prefill_workspace_bytes(const int32_t* cu_seqlens,
+                                                int32_t num_seqs,
+                                                int32_t value_heads);
+GDN_B200_API int32_t gdn_b200_chunk_prefill(const void* q, const void* k, const void* v,
+                               const void* a, const void* b,
+                               const float* A_log, const float* dt_bias,
+                               float* state, void* o_out,
+                               const int32_t* cu_seqlens, int32_t num_seqs,
+                               int32_t qk_heads, int32_t value_heads,
+                               void* workspace, uint64_t workspace_bytes,
+                               void* stream);
+
+/* Whole post-projection layer: core (decode kernel when every sequence has
+ * one token, chunk kernels otherwise) then the flattened output tail.
+ * Replaces the Submit path after the projections (P:3249-3547). */
+GDN_B200_API uint64_t gdn_b200_layer_forward_workspace_bytes(const int32_t* cu_seqlens,
+                                                int32_t num_seqs,
+                                                int32_t value_heads,
+                                                int32_t hidden);
+GDN_B200_API int32_t gdn_b200_layer_forward(const void* q, const void* k, const void* v,
+                               const void* a, const void* b, const void* z,
+                               const float* A_log, const float* dt_bias,
+                               const void* gamma, const void* w_out,
+                               float* state, void* out,
+                               const int32_t* cu_seqlens, int32_t num_seqs,
+                               int32_t qk_heads, int32_t value_heads,
+                               int32_t hidden, void* workspace,
+                               uint64_t workspace_bytes, void* stream);
+
+/* Seeded synthetic inputs (host side, used by benchmarks and tests).
+ * Element i of tensor `tensor_id` under `seed` is a pure function of
+ * (seed, tensor_id, i): SplitMix64 counters, Box-Muller for normals.
+ * distribution: 0 = normal(p0 = mean, p1 = std), 1 = uniform[p0, p1),
+ *               2 = log(uniform(p0, p1)).
+ * out_dtype: 1 = bf16 (round to nearest even), 2 = f32. */
+GDN_B200_API int32_t gdn_b200_fill_synthetic(uint64_t seed, uint64_t tensor_id,
+                                uint64_t count, int32_t distribution, float p0,
+                                float p1, int32_t out_dtype, void* host_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

@@ -1,0 +1,250 @@
+// Shared device helpers for the sm_100a GDN kernels: bf16 conversion,
+// mbarriers with bounded waits, TMA, and tcgen05 (UMMA + TMEM) wrappers.
+//
+// Every spin in this library is bounded by a wall-clock limit read from
+// %globaltimer.  A wait that runs out records an error code in the kernel's
+// error word (see GdnErrorWord) and returns false; the caller then skips the
+// rest of its work, releases TMEM and exits, so a malformed launch ends with
+// an error status on the host instead of a hung GPU.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+constexpr int kHeadDim = 128;
+constexpr int kChunk = 64;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Error codes written to the per-launch error word.
+enum : uint32_t {
+  kErrNone = 0,
+  kErrWaitTimeout = 1,
+  kErrTmemAlloc = 2,
+  kErrBadGeometry = 3,
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void record_error(uint32_t* err, uint32_t code) {
+  if (err != nullptr) atomicCAS(err, 0u, code);
+}
+
+// ------------------------------------------------------------- bf16 -----
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
+  return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+__device__ __forceinline__ float round_bf16(float f) {
+  return __bfloat162float(__float2bfloat16_rn(f));
+}
+// Two floats -> packed bf16x2 (low half = first).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return static_cast<uint32_t>(f32_to_bf16_bits(lo)) |
+         (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+}
+
+// ---------------------------------------------------------- mbarrier -----
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on a phase parity.  Returns false (and records the error) when
+// the limit runs out or another thread of the launch already failed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - start > kWaitLimitNs) {
+      record_error(err, kErrWaitTimeout);
+      return false;
+    }
+    if (err != nullptr && *reinterpret_cast<volatile uint32_t*>(err) != 0) return false;
+  }
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Orders generic-proxy shared-memory writes before async-proxy reads
+// (tcgen05.mma operands, TMA stores).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// -------------------------------------------------------------- TMA ------
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled bulk tensor load into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map,
+                                            uint64_t* bar, int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// 1-D bulk copy global -> this CTA's shared memory (no multicast).  Both
+// addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ------------------------------------------------------------ tcgen05 ----
+
+// UMMA shared-memory matrix descriptor (sm_100 layout: start >> 4 in [0,14),
+// LBO >> 4 in [16,30), SBO >> 4 in [32,46), version 1 in [46,48),
+// layout type in [61,64); 2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t umma_sdesc(uint32_t smem_addr, uint32_t lbo_bytes,
+                                               uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16 with bf16 A/B and f32 accumulator.
+// a_mn / b_mn select MN-major operands (bit 15 / 16).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | ((static_cast<uint32_t>(n) >> 3) << 17) |
+         ((static_cast<uint32_t>(m) >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` once every tcgen05 operation issued so far by this
+// thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Whole-warp TMEM allocation; the column base is written to *dst_smem.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Warp-wide TMEM load: lane i of the warp reads TMEM lane (taddr.lane + i),
+// 16 consecutive 32-bit columns starting at taddr.column.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// TMEM address of (lane, column) relative to a column base.
+__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint32_t col) {
+  return base + (lane << 16) + col;
+}
+
+// ------------------------------------------------- operand smem layouts --
+// 128-byte-swizzled canonical layouts used for every UMMA operand here.
+// A 1024-byte atom holds 8 rows of 128 bytes (64 bf16); within the atom the
+// 16-byte chunk c of row r sits at chunk position c ^ r.  Atoms must start on
+// a 1024-byte boundary.
+//
+// K-major operand of R rows (M or N) and K columns: 64-column slabs of
+// R * 128 bytes, slab s at s * R * 128; descriptor LBO = 16, SBO = 1024; the
+// K step of 16 elements adds 32 bytes inside a slab.
+__device__ __forceinline__ uint32_t kmajor_offset(uint32_t row, uint32_t col, uint32_t rows) {
+  const uint32_t slab = col >> 6;
+  const uint32_t c = col & 63u;
+  return slab * rows * 128u + (row >> 3) * 1024u + (row & 7u) * 128u +
+         ((((c >> 3) ^ (row & 7u)) & 7u) << 4) + (c & 7u) * 2u;
+}
+// MN-major operand: K rows of 64-element MN slabs.  Element (k, mn) of an
+// operand with K extent kext: slab (mn / 64) at slab * kext * 128, row k at
+// (k / 8) * 1024 + (k % 8) * 128; descriptor LBO = kext * 128 (slab stride),
+// SBO = 1024; the K step of 16 rows adds 2048 bytes.
+__device__ __forceinline__ uint32_t mnmajor_offset(uint32_t k, uint32_t mn, uint32_t kext) {
+  const uint32_t slab = mn >> 6;
+  const uint32_t c = mn & 63u;
+  return slab * kext * 128u + (k >> 3) * 1024u + (k & 7u) * 128u +
+         ((((c >> 3) ^ (k & 7u)) & 7u) << 4) + (c & 7u) * 2u;
+}
+// Byte offset of the 16-byte chunk holding elements [8j, 8j+8) of row `row`
+// in one 128-byte-swizzled slab (same formula for both majors).
+__device__ __forceinline__ uint32_t sw128_chunk(uint32_t row, uint32_t j) {
+  return (row >> 3) * 1024u + (row & 7u) * 128u + (((j ^ row) & 7u) << 4);
+}
+
+}  // namespace gdn

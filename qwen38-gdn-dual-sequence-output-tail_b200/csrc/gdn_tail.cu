@@ -1,0 +1,377 @@
+// Dual-sequence output tail: gated RMSNorm prologue + one flattened out_proj
+// GEMM on tcgen05.
+//
+// Replaces BatchGdnOutputTail (reference provider P:1434-1498; the flattened
+// Matmul of patches/0001-feat-qwen38-flatten-dual-tail-output-projection.patch
+// :179-184), LaneGdnOutputTailV13 (P:1371-1432) and the single-sequence tail
+// (P:3498-3547).  The reference runs RmsNorm, Silu, Mul and Matmul as four
+// aclnn operators with four workspace allocations; here the rows of every
+// sequence are flattened into one GEMM M = sum of rows, K = Hv*128, N = hidden.
+//
+// GEMM design (sm_100a): persistent CTAs, one per SM; warp 0 issues TMA
+// loads of 128x64 A and BNx64 B tiles (128-byte swizzle) into a 4-stage ring;
+// warp 1 issues tcgen05.mma (M=128, N=BN, K=16) from one thread with the f32
+// accumulator in TMEM (two accumulators so the epilogue of one tile overlaps
+// the main loop of the next); warps 2-5 drain TMEM with tcgen05.ld and store
+// bf16.  When there are fewer output tiles than SMs (decode rows, the 2x64
+// tail) the K dimension is split across CTAs; each split writes an f32
+// partial tile and a small pass sums the splits in a fixed order (the result
+// does not depend on scheduling) and rounds to bf16.
+#include <vector>
+
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+
+namespace gdn {
+
+// ------------------------------------------------------------ prologue --
+
+// gated[r, h*128 + j] = bf16( bf16(o*rstd*gamma) * bf16(SiLU(z)) ), one warp
+// per (row, head); the rounding points are the aclnn operator boundaries.
+__global__ void __launch_bounds__(256)
+tail_prologue_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ z,
+                     const uint16_t* __restrict__ gamma, uint16_t* __restrict__ gated,
+                     int64_t pairs, float eps) {
+  const int64_t pair = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (pair >= pairs) return;
+  const int64_t base = pair * kHeadDim + lane * 4;
+  const uint2 orow = *reinterpret_cast<const uint2*>(o + base);
+  const uint2 zrow = *reinterpret_cast<const uint2*>(z + base);
+  const uint2 grow = *reinterpret_cast<const uint2*>(gamma + lane * 4);
+  const float x[4] = {bf16_bits_to_f32(orow.x & 0xFFFFu), bf16_bits_to_f32(orow.x >> 16),
+                      bf16_bits_to_f32(orow.y & 0xFFFFu), bf16_bits_to_f32(orow.y >> 16)};
+  const float zz[4] = {bf16_bits_to_f32(zrow.x & 0xFFFFu), bf16_bits_to_f32(zrow.x >> 16),
+                       bf16_bits_to_f32(zrow.y & 0xFFFFu), bf16_bits_to_f32(zrow.y >> 16)};
+  const float gg[4] = {bf16_bits_to_f32(grow.x & 0xFFFFu), bf16_bits_to_f32(grow.x >> 16),
+                       bf16_bits_to_f32(grow.y & 0xFFFFu), bf16_bits_to_f32(grow.y >> 16)};
+  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rstd = rsqrtf(ss * (1.0f / 128.0f) + eps);
+  float r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float n = round_bf16(x[i] * rstd * gg[i]);
+    const float s = round_bf16(zz[i] / (1.0f + expf(-zz[i])));
+    r[i] = n * s;
+  }
+  uint2 w;
+  w.x = pack_bf16x2(r[0], r[1]);
+  w.y = pack_bf16x2(r[2], r[3]);
+  *reinterpret_cast<uint2*>(gated + base) = w;
+}
+
+// ---------------------------------------------------------------- GEMM --
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct GemmSmem {
+  static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;
+  static constexpr uint32_t kBBytes = BN * kGemmBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarrierOffset = kGemmStages * kStageBytes;
+  static constexpr uint32_t kTotal = kBarrierOffset + 256 + 1024;  // + alignment slack
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+tail_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                 const __grid_constant__ CUtensorMap tmap_b, uint16_t* __restrict__ out,
+                 float* __restrict__ out_f32, int M, int N, int tiles_m, int tiles_n, int splits,
+                 int kblocks_total, int kblocks_per_split, uint32_t* err) {
+  using L = GemmSmem<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
+  uint64_t* empty = full + kGemmStages;
+  uint64_t* tfull = empty + kGemmStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total_units = tiles_m * tiles_n * splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], 128);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
+        const int split = unit % splits;
+        const int tile = unit / splits;
+        const int tn = tile % tiles_n;
+        const int tm = tile / tiles_n;
+        const int kb0 = split * kblocks_per_split;
+        const int kb1 = min(kb0 + kblocks_per_split, kblocks_total);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          uint8_t* sa = smem + stage * L::kStageBytes;
+          tma_load_2d(sa, &tmap_a, &full[stage], kb * kGemmBK, tm * kGemmBM);
+          tma_load_2d(sa + L::kABytes, &tmap_b, &full[stage], kb * kGemmBK, tn * BN);
+          if (++stage == kGemmStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kGemmBM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
+        const int split = unit % splits;
+        const int kb0 = split * kblocks_per_split;
+        const int kb1 = min(kb0 + kblocks_per_split, kblocks_total);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err)) break;
+        tmem_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err)) { ok = false; break; }
+          tmem_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+            umma_bf16(d, umma_sdesc(sa + kk * 32, 16, 1024), umma_sdesc(sb + kk * 32, 16, 1024),
+                      idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == kGemmStages) { stage = 0; phase ^= 1u; }
+        }
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // Epilogue warps 2..5: warp w drains TMEM lanes 32*(w%4) .. +31.
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x) {
+      const int tile = unit / splits;
+      const int tn = tile % tiles_n;
+      const int tm = tile / tiles_n;
+      if (!mbar_wait(&tfull[acc], acc_phase, err)) break;
+      tmem_fence_after();
+      const int row = tm * kGemmBM + quarter * 32 + lane;
+      const uint32_t tbase = tmem_addr(tmem_base, quarter * 32, acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(tbase + c, r);
+        tmem_ld_wait();
+        if (row < M) {
+          const int64_t off = static_cast<int64_t>(row) * N + tn * BN + c;
+          if (splits == 1) {
+            uint4 w0, w1;
+            w0.x = pack_bf16x2(__uint_as_float(r[0]), __uint_as_float(r[1]));
+            w0.y = pack_bf16x2(__uint_as_float(r[2]), __uint_as_float(r[3]));
+            w0.z = pack_bf16x2(__uint_as_float(r[4]), __uint_as_float(r[5]));
+            w0.w = pack_bf16x2(__uint_as_float(r[6]), __uint_as_float(r[7]));
+            w1.x = pack_bf16x2(__uint_as_float(r[8]), __uint_as_float(r[9]));
+            w1.y = pack_bf16x2(__uint_as_float(r[10]), __uint_as_float(r[11]));
+            w1.z = pack_bf16x2(__uint_as_float(r[12]), __uint_as_float(r[13]));
+            w1.w = pack_bf16x2(__uint_as_float(r[14]), __uint_as_float(r[15]));
+            reinterpret_cast<uint4*>(out + off)[0] = w0;
+            reinterpret_cast<uint4*>(out + off)[1] = w1;
+          } else {
+            // Split-K partial: slice `split` of the [splits, M, N] f32 scratch,
+            // summed in a fixed order afterwards (deterministic).
+            const int split = unit % splits;
+            float4* dst = reinterpret_cast<float4*>(out_f32 + static_cast<int64_t>(split) * M * N + off);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            }
+          }
+        }
+      }
+      tmem_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tmem_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// out = bf16(sum over splits of ws[split]) in split order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, uint16_t* __restrict__ out,
+                                     int64_t n4, int splits) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  float4 acc = reinterpret_cast<const float4*>(ws)[i];
+  for (int s = 1; s < splits; ++s) {
+    const float4 v = reinterpret_cast<const float4*>(ws)[s * n4 + i];
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  uint2 w;
+  w.x = pack_bf16x2(acc.x, acc.y);
+  w.y = pack_bf16x2(acc.z, acc.w);
+  reinterpret_cast<uint2*>(out)[i] = w;
+}
+
+// ------------------------------------------------------------- host side --
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+  }
+  return fn;
+}
+
+// Row-major bf16 matrix [rows, cols] (cols contiguous), box [box_rows, 64]
+// with 128-byte swizzle; rows beyond the matrix read as zero.
+static bool make_tmap_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
+                           int box_rows) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+struct TailGemmPlan {
+  int bn, tiles_m, tiles_n, splits, kblocks_total, kblocks_per_split, grid;
+};
+
+static int sm_count() {
+  static int count = 0;
+  if (count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        count <= 0)
+      count = 148;
+  }
+  return count;
+}
+
+TailGemmPlan plan_tail_gemm(int64_t M, int N, int K) {
+  TailGemmPlan p{};
+  p.bn = (N % 256 == 0) ? 256 : 128;
+  p.tiles_m = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
+  p.tiles_n = N / p.bn;
+  p.kblocks_total = K / kGemmBK;
+  const int sms = sm_count();
+  const int tiles = p.tiles_m * p.tiles_n;
+  p.splits = 1;
+  if (tiles * 2 <= sms) {
+    int want = sms / tiles;
+    if (want > p.kblocks_total) want = p.kblocks_total;
+    // keep at least 2 k-blocks per split so TMA and MMA overlap
+    while (want > 1 && p.kblocks_total / want < 2) --want;
+    p.splits = want;
+  }
+  p.kblocks_per_split = (p.kblocks_total + p.splits - 1) / p.splits;
+  p.splits = (p.kblocks_total + p.kblocks_per_split - 1) / p.kblocks_per_split;
+  const int units = tiles * p.splits;
+  p.grid = units < sms ? units : sms;
+  return p;
+}
+
+uint64_t tail_gemm_workspace_bytes(int64_t M, int N, int K) {
+  const TailGemmPlan p = plan_tail_gemm(M, N, K);
+  return p.splits > 1 ? static_cast<uint64_t>(p.splits) * M * N * sizeof(float) : 0;
+}
+
+cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uint16_t* gamma,
+                                 uint16_t* gated, int64_t rows, int value_heads, float eps,
+                                 cudaStream_t stream) {
+  const int64_t pairs = rows * value_heads;
+  if (pairs == 0) return cudaSuccess;
+  const int64_t blocks = (pairs + 7) / 8;
+  tail_prologue_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(o, z, gamma, gated,
+                                                                          pairs, eps);
+  return cudaGetLastError();
+}
+
+template <int BN>
+static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, uint16_t* out,
+                                  float* ws, int64_t M, int N, const TailGemmPlan& p,
+                                  uint32_t* err, cudaStream_t stream) {
+  const uint32_t smem = GemmSmem<BN>::kTotal;
+  cudaError_t e = cudaFuncSetAttribute(tail_gemm_kernel<BN>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  tail_gemm_kernel<BN><<<p.grid, kGemmThreads, smem, stream>>>(
+      ta, tb, out, ws, static_cast<int>(M), N, p.tiles_m, p.tiles_n, p.splits, p.kblocks_total,
+      p.kblocks_per_split, err);
+  return cudaGetLastError();
+}
+
+// out[M, N] = a[M, K] @ w[N, K]^T  (bf16 in, f32 accumulate, bf16 out).
+// ws: f32 [M, N] scratch when the plan splits K (tail_gemm_workspace_bytes).
+cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out, float* ws,
+                             int64_t M, int N, int K, uint32_t* err, cudaStream_t stream) {
+  if (M == 0) return cudaSuccess;
+  const TailGemmPlan p = plan_tail_gemm(M, N, K);
+  CUtensorMap ta, tb;
+  if (!make_tmap_bf16(&ta, a, M, K, kGemmBM) || !make_tmap_bf16(&tb, w, N, K, p.bn))
+    return cudaErrorInvalidValue;
+  cudaError_t e = (p.bn == 256) ? launch_gemm_bn<256>(ta, tb, out, ws, M, N, p, err, stream)
+                                : launch_gemm_bn<128>(ta, tb, out, ws, M, N, p, err, stream);
+  if (e != cudaSuccess) return e;
+  if (p.splits > 1) {
+    const int64_t n4 = M * N / 4;
+    splitk_reduce_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(ws, out, n4,
+                                                                                   p.splits);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+}  // namespace gdn
