@@ -90,8 +90,9 @@ GDN_B200_API int32_t gdn_b200_decode_step(const void* q, const void* k, const vo
  * Replaces ChunkGdn (P:1641-1838) and the token-serial run_sequence
  * (P:3387-3469): every sequence length, any number of chunks, one call. */
 GDN_B200_API uint64_t gdn_b200_chunk_prefill_workspace_bytes(const int32_t* cu_seqlens,
-                                                int32_t num_seqs,
-                                                int32_t value_heads);
+                                                             int32_t num_seqs,
+                                                             int32_t qk_heads,
+                                                             int32_t value_heads);
 GDN_B200_API int32_t gdn_b200_chunk_prefill(const void* q, const void* k, const void* v,
                                const void* a, const void* b,
                                const float* A_log, const float* dt_bias,
@@ -105,9 +106,10 @@ GDN_B200_API int32_t gdn_b200_chunk_prefill(const void* q, const void* k, const 
  * one token, chunk kernels otherwise) then the flattened output tail.
  * Replaces the Submit path after the projections (P:3249-3547). */
 GDN_B200_API uint64_t gdn_b200_layer_forward_workspace_bytes(const int32_t* cu_seqlens,
-                                                int32_t num_seqs,
-                                                int32_t value_heads,
-                                                int32_t hidden);
+                                                             int32_t num_seqs,
+                                                             int32_t qk_heads,
+                                                             int32_t value_heads,
+                                                             int32_t hidden);
 GDN_B200_API int32_t gdn_b200_layer_forward(const void* q, const void* k, const void* v,
                                const void* a, const void* b, const void* z,
                                const float* A_log, const float* dt_bias,

@@ -103,7 +103,7 @@ int32_t gdn_b200_output_tail(const void* o, const void* z, const void* gamma, co
       workspace == nullptr)
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
   if (!aligned16(o) || !aligned16(z) || !aligned16(w_out) || !aligned16(out) ||
-      !aligned16(workspace) || (reinterpret_cast<uintptr_t>(gamma) & 7u) != 0)
+      !aligned16(workspace) || !aligned16(gamma))
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
   const uint64_t need = gdn_b200_output_tail_workspace_bytes(rows, value_heads, hidden);
   if (workspace_bytes < need)
@@ -163,23 +163,24 @@ int32_t gdn_b200_decode_step(const void* q, const void* k, const void* v, const 
 // ------------------------------------------------------------ chunk ----
 
 uint64_t gdn_b200_chunk_prefill_workspace_bytes(const int32_t* cu_seqlens, int32_t num_seqs,
-                                                int32_t value_heads) {
+                                                int32_t qk_heads, int32_t value_heads) {
   gdn::ChunkTable tab;
-  if (value_heads <= 0 || check_seqlens(cu_seqlens, num_seqs, &tab) != STATECENTRIC_QWEN38_OK)
+  if (!heads_ok(qk_heads, value_heads) ||
+      check_seqlens(cu_seqlens, num_seqs, &tab) != STATECENTRIC_QWEN38_OK)
     return 0;
-  return kErrBytes + round256(gdn::chunk_workspace_bytes(tab, value_heads));
+  return kErrBytes + round256(gdn::chunk_workspace_bytes(tab, qk_heads, value_heads));
 }
 
 static int32_t chunk_prefill_impl(const gdn::ChunkTable& tab, const void* q, const void* k,
                                   const void* v, const void* a, const void* b,
                                   const float* A_log, const float* dt_bias, float* state,
                                   void* o_out, int32_t qk_heads, int32_t value_heads,
-                                  uint8_t* records, uint32_t* err, cudaStream_t s) {
+                                  uint8_t* scratch, uint32_t* err, cudaStream_t s) {
   cudaError_t e = gdn::launch_chunk_prefill(
       tab, static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
       static_cast<const uint16_t*>(v), static_cast<const uint16_t*>(a),
       static_cast<const uint16_t*>(b), A_log, dt_bias, state, static_cast<uint16_t*>(o_out),
-      qk_heads, value_heads, records, err, s);
+      qk_heads, value_heads, scratch, err, s);
   return cuda_status(e, "chunk prefill launch");
 }
 
@@ -201,7 +202,7 @@ int32_t gdn_b200_chunk_prefill(const void* q, const void* k, const void* v, cons
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o_out) ||
       !aligned16(state) || !aligned16(workspace))
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
-  const uint64_t need = kErrBytes + round256(gdn::chunk_workspace_bytes(tab, value_heads));
+  const uint64_t need = kErrBytes + round256(gdn::chunk_workspace_bytes(tab, qk_heads, value_heads));
   if (workspace_bytes < need)
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT,
                 "workspace too small: need " + std::to_string(need) + " bytes");
@@ -223,9 +224,10 @@ static bool all_single_token(const gdn::ChunkTable& tab) {
 }
 
 uint64_t gdn_b200_layer_forward_workspace_bytes(const int32_t* cu_seqlens, int32_t num_seqs,
-                                                int32_t value_heads, int32_t hidden) {
+                                                int32_t qk_heads, int32_t value_heads,
+                                                int32_t hidden) {
   gdn::ChunkTable tab;
-  if (value_heads <= 0 || hidden <= 0 ||
+  if (!heads_ok(qk_heads, value_heads) || hidden <= 0 ||
       check_seqlens(cu_seqlens, num_seqs, &tab) != STATECENTRIC_QWEN38_OK)
     return 0;
   const int64_t T = tab.cu[num_seqs];
@@ -233,7 +235,8 @@ uint64_t gdn_b200_layer_forward_workspace_bytes(const int32_t* cu_seqlens, int32
   uint64_t bytes = kErrBytes;
   bytes += round256(static_cast<uint64_t>(T) * K * 2);  // o
   bytes += round256(static_cast<uint64_t>(T) * K * 2);  // gated
-  if (!all_single_token(tab)) bytes += round256(gdn::chunk_workspace_bytes(tab, value_heads));
+  if (!all_single_token(tab))
+    bytes += round256(gdn::chunk_workspace_bytes(tab, qk_heads, value_heads));
   bytes += round256(gdn::tail_gemm_workspace_bytes(T, hidden, static_cast<int>(K)));
   return bytes;
 }
@@ -259,10 +262,10 @@ int32_t gdn_b200_layer_forward(const void* q, const void* k, const void* v, cons
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(z) || !aligned16(w_out) ||
       !aligned16(out) || !aligned16(state) || !aligned16(workspace) ||
-      (reinterpret_cast<uintptr_t>(gamma) & 7u) != 0)
+      !aligned16(gamma))
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
   const uint64_t need =
-      gdn_b200_layer_forward_workspace_bytes(cu_seqlens, num_seqs, value_heads, hidden);
+      gdn_b200_layer_forward_workspace_bytes(cu_seqlens, num_seqs, qk_heads, value_heads, hidden);
   if (workspace_bytes < need)
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT,
                 "workspace too small: need " + std::to_string(need) + " bytes");
@@ -278,7 +281,7 @@ int32_t gdn_b200_layer_forward(const void* q, const void* k, const void* v, cons
   off += round256(static_cast<uint64_t>(T) * K * 2);
   const bool decode = all_single_token(tab);
   uint8_t* records = ws + off;
-  if (!decode) off += round256(gdn::chunk_workspace_bytes(tab, value_heads));
+  if (!decode) off += round256(gdn::chunk_workspace_bytes(tab, qk_heads, value_heads));
   float* gemm_ws = reinterpret_cast<float*>(ws + off);
 
   cudaError_t e = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);

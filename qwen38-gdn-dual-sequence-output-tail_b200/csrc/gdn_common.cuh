@@ -2,8 +2,8 @@
 // mbarriers with bounded waits, TMA, and tcgen05 (UMMA + TMEM) wrappers.
 //
 // Every spin in this library is bounded by a wall-clock limit read from
-// %globaltimer.  A wait that runs out records an error code in the kernel's
-// error word (see GdnErrorWord) and returns false; the caller then skips the
+// %globaltimer.  A wait that runs out records an error code in the error
+// word the kernel was given and returns false; the caller then skips the
 // rest of its work, releases TMEM and exits, so a malformed launch ends with
 // an error status on the host instead of a hung GPU.
 #pragma once
@@ -49,13 +49,29 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
 __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
+// Round to the nearest bf16 value (ties to even), result as f32.  Integer
+// arithmetic keeps this off the transcendental/conversion pipe; inputs are
+// finite (NaN payloads are not preserved).
 __device__ __forceinline__ float round_bf16(float f) {
-  return __bfloat162float(__float2bfloat16_rn(f));
+  uint32_t u = __float_as_uint(f);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return __uint_as_float(u & 0xFFFF0000u);
 }
-// Two floats -> packed bf16x2 (low half = first).
+// Two floats -> packed bf16x2 (round to nearest even; low half = first),
+// one cvt.rn.bf16x2.f32.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return static_cast<uint32_t>(f32_to_bf16_bits(lo)) |
-         (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Low / high bf16 of a packed pair, as f32.
+__device__ __forceinline__ float bf16lo_f32(uint32_t p) { return __uint_as_float(p << 16); }
+__device__ __forceinline__ float bf16hi_f32(uint32_t p) { return __uint_as_float(p & 0xFFFF0000u); }
+// x ~= hi + lo with hi = bf16(x), lo = bf16(x - hi): two bf16 operands that
+// carry about 16 mantissa bits of x.  Returns packed (hi0,hi1) and (lo0,lo1).
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16x2(x0, x1);
+  lo = pack_bf16x2(x0 - bf16lo_f32(hi), x1 - bf16hi_f32(hi));
 }
 
 // ---------------------------------------------------------- mbarrier -----

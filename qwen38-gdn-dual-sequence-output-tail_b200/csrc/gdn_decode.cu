@@ -136,7 +136,7 @@ gdn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float n = round_bf16(x[i] * rstd * gg[i]);
-        const float sl = round_bf16(zz[i] / (1.0f + expf(-zz[i])));
+        const float sl = round_bf16(__fdividef(zz[i], 1.0f + __expf(-zz[i])));
         out[i] = n * sl;
       }
       uint2 w;

@@ -16,12 +16,12 @@ struct ChunkTable {
 };
 
 bool build_chunk_table(const int32_t* cu_seqlens, int num_seqs, ChunkTable* tab);
-uint64_t chunk_workspace_bytes(const ChunkTable& tab, int value_heads);
+uint64_t chunk_workspace_bytes(const ChunkTable& tab, int qk_heads, int value_heads);
 cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const uint16_t* k,
                                  const uint16_t* v, const uint16_t* a, const uint16_t* b,
                                  const float* A_log, const float* dt_bias, float* state,
                                  uint16_t* o_out, int qk_heads, int value_heads,
-                                 uint8_t* records, uint32_t* err, cudaStream_t stream);
+                                 uint8_t* scratch, uint32_t* err, cudaStream_t stream);
 
 cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                           const uint16_t* a, const uint16_t* b, const float* A_log,

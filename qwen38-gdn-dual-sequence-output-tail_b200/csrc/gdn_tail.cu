@@ -26,40 +26,48 @@ namespace gdn {
 
 // ------------------------------------------------------------ prologue --
 
-// gated[r, h*128 + j] = bf16( bf16(o*rstd*gamma) * bf16(SiLU(z)) ), one warp
-// per (row, head); the rounding points are the aclnn operator boundaries.
+// gated[r, h*128 + j] = bf16( bf16(o*rstd*gamma) * bf16(SiLU(z)) ); the
+// rounding points are the aclnn operator boundaries.  Sixteen threads per
+// (row, head), eight elements (16 bytes) each.
 __global__ void __launch_bounds__(256)
 tail_prologue_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ z,
                      const uint16_t* __restrict__ gamma, uint16_t* __restrict__ gated,
                      int64_t pairs, float eps) {
-  const int64_t pair = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (pair >= pairs) return;
-  const int64_t base = pair * kHeadDim + lane * 4;
-  const uint2 orow = *reinterpret_cast<const uint2*>(o + base);
-  const uint2 zrow = *reinterpret_cast<const uint2*>(z + base);
-  const uint2 grow = *reinterpret_cast<const uint2*>(gamma + lane * 4);
-  const float x[4] = {bf16_bits_to_f32(orow.x & 0xFFFFu), bf16_bits_to_f32(orow.x >> 16),
-                      bf16_bits_to_f32(orow.y & 0xFFFFu), bf16_bits_to_f32(orow.y >> 16)};
-  const float zz[4] = {bf16_bits_to_f32(zrow.x & 0xFFFFu), bf16_bits_to_f32(zrow.x >> 16),
-                       bf16_bits_to_f32(zrow.y & 0xFFFFu), bf16_bits_to_f32(zrow.y >> 16)};
-  const float gg[4] = {bf16_bits_to_f32(grow.x & 0xFFFFu), bf16_bits_to_f32(grow.x >> 16),
-                       bf16_bits_to_f32(grow.y & 0xFFFFu), bf16_bits_to_f32(grow.y >> 16)};
-  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+  const int64_t pair = static_cast<int64_t>(blockIdx.x) * 16 + (threadIdx.x >> 4);
+  const int sub = threadIdx.x & 15;
+  const bool live = pair < pairs;
+  const int64_t base = (live ? pair : 0) * kHeadDim + sub * 8;
+  const uint4 ov = *reinterpret_cast<const uint4*>(o + base);
+  const uint4 zv = *reinterpret_cast<const uint4*>(z + base);
+  const uint4 gv = *reinterpret_cast<const uint4*>(gamma + sub * 8);
+  const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
+  const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
+  const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+  float ss = 0.f;
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  const float rstd = rsqrtf(ss * (1.0f / 128.0f) + eps);
-  float r[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float n = round_bf16(x[i] * rstd * gg[i]);
-    const float s = round_bf16(zz[i] / (1.0f + expf(-zz[i])));
-    r[i] = n * s;
+  for (int p = 0; p < 4; ++p) {
+    const float x0 = bf16lo_f32(ow[p]), x1 = bf16hi_f32(ow[p]);
+    ss += x0 * x0 + x1 * x1;
   }
-  uint2 w;
-  w.x = pack_bf16x2(r[0], r[1]);
-  w.y = pack_bf16x2(r[2], r[3]);
-  *reinterpret_cast<uint2*>(gated + base) = w;
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rstd = rsqrtf(ss * (1.0f / 128.0f) + eps);
+  uint32_t res[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    float r2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float x = e ? bf16hi_f32(ow[p]) : bf16lo_f32(ow[p]);
+      const float zz = e ? bf16hi_f32(zw[p]) : bf16lo_f32(zw[p]);
+      const float gg = e ? bf16hi_f32(gw[p]) : bf16lo_f32(gw[p]);
+      const float nrm = round_bf16(x * rstd * gg);
+      const float sl = round_bf16(__fdividef(zz, 1.0f + __expf(-zz)));
+      r2[e] = nrm * sl;
+    }
+    res[p] = pack_bf16x2(r2[0], r2[1]);
+  }
+  if (live) *reinterpret_cast<uint4*>(gated + base) = make_uint4(res[0], res[1], res[2], res[3]);
 }
 
 // ---------------------------------------------------------------- GEMM --
@@ -333,7 +341,7 @@ cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uin
                                  cudaStream_t stream) {
   const int64_t pairs = rows * value_heads;
   if (pairs == 0) return cudaSuccess;
-  const int64_t blocks = (pairs + 7) / 8;
+  const int64_t blocks = (pairs + 15) / 16;
   tail_prologue_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(o, z, gamma, gated,
                                                                           pairs, eps);
   return cudaGetLastError();

@@ -78,11 +78,11 @@ def lib() -> ctypes.CDLL:
         L.gdn_b200_output_tail.restype = i32
         L.gdn_b200_decode_step.argtypes = [vp] * 12 + [i32, i32, i32, vp]
         L.gdn_b200_decode_step.restype = i32
-        L.gdn_b200_chunk_prefill_workspace_bytes.argtypes = [i32p, i32, i32]
+        L.gdn_b200_chunk_prefill_workspace_bytes.argtypes = [i32p, i32, i32, i32]
         L.gdn_b200_chunk_prefill_workspace_bytes.restype = u64
         L.gdn_b200_chunk_prefill.argtypes = [vp] * 9 + [i32p, i32, i32, i32, vp, u64, vp]
         L.gdn_b200_chunk_prefill.restype = i32
-        L.gdn_b200_layer_forward_workspace_bytes.argtypes = [i32p, i32, i32, i32]
+        L.gdn_b200_layer_forward_workspace_bytes.argtypes = [i32p, i32, i32, i32, i32]
         L.gdn_b200_layer_forward_workspace_bytes.restype = u64
         L.gdn_b200_layer_forward.argtypes = [vp] * 12 + [i32p, i32, i32, i32, i32, vp, u64, vp]
         L.gdn_b200_layer_forward.restype = i32
@@ -153,9 +153,10 @@ def decode_step(q, k, v, a, b, A_log, dt_bias, state, o_out=None, z=None, gamma=
                                       _stream(stream)))
 
 
-def chunk_prefill_workspace_bytes(cu_seqlens, value_heads: int) -> int:
+def chunk_prefill_workspace_bytes(cu_seqlens, qk_heads: int, value_heads: int) -> int:
     arr, p = _cu_array(cu_seqlens)
-    return int(lib().gdn_b200_chunk_prefill_workspace_bytes(p, len(arr) - 1, value_heads))
+    return int(lib().gdn_b200_chunk_prefill_workspace_bytes(p, len(arr) - 1, qk_heads,
+                                                            value_heads))
 
 
 def chunk_prefill(q, k, v, a, b, A_log, dt_bias, state, cu_seqlens, o_out=None,
@@ -166,7 +167,7 @@ def chunk_prefill(q, k, v, a, b, A_log, dt_bias, state, cu_seqlens, o_out=None,
     if o_out is None:
         o_out = torch.empty_like(v)
     if workspace is None:
-        workspace = _workspace(chunk_prefill_workspace_bytes(arr, hv), q.device)
+        workspace = _workspace(chunk_prefill_workspace_bytes(arr, hk, hv), q.device)
     _check(lib().gdn_b200_chunk_prefill(_ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b),
                                         _ptr(A_log), _ptr(dt_bias), _ptr(state), _ptr(o_out), p,
                                         len(arr) - 1, hk, hv, _ptr(workspace), workspace.numel(),
@@ -174,10 +175,11 @@ def chunk_prefill(q, k, v, a, b, A_log, dt_bias, state, cu_seqlens, o_out=None,
     return o_out
 
 
-def layer_forward_workspace_bytes(cu_seqlens, value_heads: int, hidden: int) -> int:
+def layer_forward_workspace_bytes(cu_seqlens, qk_heads: int, value_heads: int,
+                                  hidden: int) -> int:
     arr, p = _cu_array(cu_seqlens)
-    return int(lib().gdn_b200_layer_forward_workspace_bytes(p, len(arr) - 1, value_heads,
-                                                            hidden))
+    return int(lib().gdn_b200_layer_forward_workspace_bytes(p, len(arr) - 1, qk_heads,
+                                                            value_heads, hidden))
 
 
 def layer_forward(q, k, v, a, b, z, A_log, dt_bias, gamma, w_out, state, cu_seqlens,
@@ -189,7 +191,7 @@ def layer_forward(q, k, v, a, b, z, A_log, dt_bias, gamma, w_out, state, cu_seql
     if out is None:
         out = torch.empty(q.shape[0], hidden, dtype=torch.bfloat16, device=q.device)
     if workspace is None:
-        workspace = _workspace(layer_forward_workspace_bytes(arr, hv, hidden), q.device)
+        workspace = _workspace(layer_forward_workspace_bytes(arr, hk, hv, hidden), q.device)
     _check(lib().gdn_b200_layer_forward(_ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), _ptr(z),
                                         _ptr(A_log), _ptr(dt_bias), _ptr(gamma), _ptr(w_out),
                                         _ptr(state), _ptr(out), p, len(arr) - 1, hk, hv, hidden,

@@ -126,7 +126,7 @@ def test_chunk_prefill_matches_oracle(cuda, cu, a_log_hi, state_std):
     x = G.synthetic_layer_inputs(cu, geom, seed=3, state_std=state_std, a_log_hi=a_log_hi)
     ref_o, ref_state = oracle_core(x, cu)
     t = G.to_device(x, cuda)
-    ws = torch.empty(G.chunk_prefill_workspace_bytes(cu, geom.value_heads), dtype=torch.uint8,
+    ws = torch.empty(G.chunk_prefill_workspace_bytes(cu, geom.qk_heads, geom.value_heads), dtype=torch.uint8,
                      device=cuda)
     o = G.chunk_prefill(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"], t["dt_bias"],
                         t["state"], cu, workspace=ws)
@@ -148,7 +148,7 @@ def test_layer_forward_matches_oracle(cuda, cu, state_std):
     ref_out = O.layer(x["q"], x["k"], x["v"], x["a"], x["b"], x["z"], x["A_log"], x["dt_bias"],
                       x["gamma"], x["w_out"], st, cu, mode=0)
     t = G.to_device(x, cuda)
-    ws = torch.empty(G.layer_forward_workspace_bytes(cu, geom.value_heads, geom.hidden),
+    ws = torch.empty(G.layer_forward_workspace_bytes(cu, geom.qk_heads, geom.value_heads, geom.hidden),
                      dtype=torch.uint8, device=cuda)
     out = G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
                           t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu, workspace=ws)
