@@ -1,0 +1,350 @@
+#!/usr/bin/env python
+"""GDN layer throughput on B200: chunked prefill of 2 x 4096 tokens (Qwen3-Next
+geometry: 16 q/k heads, 32 v heads, head dim 128, hidden 2048) followed by the
+flattened gated-RMSNorm + out_proj tail, in tokens/s.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One process per GPU (torchrun for N > 1).  With N GPUs the heads are split
+evenly across ranks (head-parallel; rank r holds v-heads [r*32/N, (r+1)*32/N)
+and the matching q/k heads and out_proj columns) and every rank processes 2*N
+sequences of 4096 tokens, so the per-rank kernel work is that of one GPU
+("weak" scaling); the rank-partial [tokens, 2048] outputs are summed with a
+bf16 NCCL all-reduce inside the timed region.  One JSON line is printed by
+rank 0.
+
+``--impl reference`` times the CPU restatement of the reference path (the
+oracle; the reference itself runs only on Ascend NPUs) on the host cores with
+the same metric and workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "qwen38-gdn-dual-sequence-output-tail_b200")
+sys.path.insert(0, PKG)
+
+METRIC = "GDN layer tokens/sec (chunked prefill 2x4096 + output tail)"
+UNIT = "tokens/s"
+SEQ_LEN = 4096
+SEQS_PER_GPU = 2
+QK_HEADS, V_HEADS, HIDDEN = 16, 32, 2048
+CHUNK_MFLOP = 11.62    # prefill core work per (chunk of 64, v-head)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        self.file.flush()
+
+    def summary(self):
+        try:
+            with open(self.file.name) as f:
+                rows = [r.split(",") for r in f.read().strip().splitlines() if r.strip()]
+            os.unlink(self.file.name)
+        except Exception:
+            rows = []
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for i, name in enumerate(names):
+                    if r[5 + i].strip().lower() == "active":
+                        reasons.add(name)
+            except Exception:
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": mx or None, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def workload_desc(nseq: int) -> str:
+    return (f"chunked prefill {nseq}x{SEQ_LEN} tokens + flattened output tail, "
+            f"Hk={QK_HEADS} Hv={V_HEADS} D=128 hidden={HIDDEN}, chunk 64")
+
+
+def cpu_oracle_prefill(seq_len: int, nseq: int, threads: int | None = None):
+    """Runs the CPU oracle (restatement of the reference's op sequence) on the
+    prefill workload; returns (tokens/s, seconds, threads)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    if threads:
+        os.environ["OMP_NUM_THREADS"] = str(threads)
+    import gdn_oracle as O
+    import gdn_b200 as G
+    geom = G.Geometry(QK_HEADS, V_HEADS, HIDDEN)
+    cu = np.arange(nseq + 1, dtype=np.int32) * seq_len
+    x = G.synthetic_layer_inputs(cu, geom, seed=1)
+    st = x["state"].copy()
+    t0 = time.perf_counter()
+    O.layer(x["q"], x["k"], x["v"], x["a"], x["b"], x["z"], x["A_log"], x["dt_bias"],
+            x["gamma"], x["w_out"], st, cu, mode=0)
+    dt = time.perf_counter() - t0
+    return (nseq * seq_len) / dt, dt, O.threads()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    nseq = SEQS_PER_GPU * args.gpus
+    for _ in range(args.warmup):
+        cpu_oracle_prefill(SEQ_LEN, SEQS_PER_GPU)
+    times = []
+    threads = 1
+    for _ in range(args.steps):
+        _, dt, threads = cpu_oracle_prefill(SEQ_LEN, SEQS_PER_GPU)
+        times.append(dt)
+    step = statistics.median(times)
+    value = SEQS_PER_GPU * SEQ_LEN / step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": workload_desc(nseq), "tokens_per_step": nseq * SEQ_LEN,
+                   "sequences": nseq, "seq_len": SEQ_LEN},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{SEQS_PER_GPU}x{SEQ_LEN} tokens of the "
+                                   f"{nseq}x{SEQ_LEN} workload per step"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import gdn_b200 as G
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    if V_HEADS % world or QK_HEADS % world:
+        raise SystemExit("heads must split evenly")
+
+    hk, hv = QK_HEADS // world, V_HEADS // world
+    geom = G.Geometry(hk, hv, HIDDEN)
+    nseq = SEQS_PER_GPU * world
+    cu = np.arange(nseq + 1, dtype=np.int32) * SEQ_LEN
+    T = int(cu[-1])
+    # Seeded synthetic inputs with the benchmark distributions for this
+    # rank's head shard (tensor ids offset per rank).
+    x = G.synthetic_layer_inputs(cu, geom, seed=1 + 1000 * rank)
+    host = {}
+    for n in ("q", "k", "v", "a", "b", "z"):
+        arr = x[n]
+        t = torch.from_numpy(arr.view(np.int16)).view(torch.bfloat16)
+        host[n] = t.pin_memory()
+    t = G.to_device(x, dev)
+    out = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(G.layer_forward_workspace_bytes(cu, hk, hv, HIDDEN), dtype=torch.uint8,
+                     device=dev)
+    # A dedicated stream: the provider ABI rejects the null stream, as the
+    # reference does (qwen38_geometry_normalized_gdn_provider.cpp:2272).
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+
+    def step():
+        G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
+                        t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu, out=out,
+                        workspace=ws, stream=stream)
+        if world > 1:
+            dist.all_reduce(out)
+
+    def timed(fn, iters, warm):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(iters):
+            fn()
+        e.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = s.elapsed_time(e) / iters
+        if world > 1:
+            v = torch.tensor([ms], device=dev)
+            dist.all_reduce(v, op=dist.ReduceOp.MAX)
+            ms = float(v.item())
+        return ms
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    G.workspace_status(ws)
+    with ClockSampler(local) as clocks:
+        ms = timed(step, args.steps, 0)
+    clk = clocks.summary()
+    G.workspace_status(ws)
+    tokens_total = T  # every rank sees all tokens of its shard; tokens are not duplicated
+    value = tokens_total / (ms * 1e-3)
+
+    # Components, timed alone with CUDA events on the launching stream:
+    # the chunked core (prep + state kernels) and the output tail.
+    o = torch.empty_like(t["v"])
+    ws_core = torch.empty(G.chunk_prefill_workspace_bytes(cu, hk, hv), dtype=torch.uint8,
+                          device=dev)
+    ws_tail = torch.empty(G.output_tail_workspace_bytes(T, hv, HIDDEN), dtype=torch.uint8,
+                          device=dev)
+    core_ms = timed(lambda: G.chunk_prefill(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"],
+                                            t["dt_bias"], t["state"], cu, o_out=o,
+                                            workspace=ws_core, stream=stream), args.steps, 2)
+    tail_ms = timed(lambda: G.output_tail(o, t["z"], t["gamma"], t["w_out"], out=out,
+                                          workspace=ws_tail, stream=stream), args.steps, 2)
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    chunks = nseq * (SEQ_LEN // 64)
+    core_flop = CHUNK_MFLOP * 1e6 * chunks * hv
+    tail_flop = 2.0 * T * (hv * 128) * HIDDEN
+    core_tf = core_flop / (core_ms * 1e-3) / 1e12
+    tail_tf = tail_flop / (tail_ms * 1e-3) / 1e12
+    comps = {
+        "chunk_core": {"ms": core_ms, "tflops": core_tf, "frac": core_tf / tf_peak},
+        "output_tail": {"ms": tail_ms, "tflops": tail_tf, "frac": tail_tf / tf_peak},
+    }
+    dom = "chunk_core" if core_ms >= tail_ms else "output_tail"
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": comps[dom]["tflops"],
+                "peak": tf_peak, "unit": "TFLOP/s", "frac": comps[dom]["frac"],
+                "peak_kind": f"{peak_kind} burst bf16", "traffic": None}
+
+    # End to end through the provider ABI (the reference-facing plugin
+    # interface): pinned host inputs -> device, submit, wait, output -> host.
+    prov = G.Provider(geom, max_tokens=T, world_size=world, rank=rank, device=local)
+    host_out = torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step():
+        for n in host:
+            t[n].copy_(host[n], non_blocking=True)
+        ev = prov.submit_layer(t, t["state"], out, cu, stream=stream)
+        prov.wait(ev)
+        prov.release(ev)
+        if world > 1:
+            dist.all_reduce(out)
+        host_out.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_iters = max(3, args.steps // 4)
+    t0 = time.perf_counter()
+    for _ in range(e2e_iters):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / e2e_iters
+    if world > 1:
+        v = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        e2e_s = float(v.item())
+    prov.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cps, csec, cthreads = cpu_oracle_prefill(SEQ_LEN, SEQS_PER_GPU)
+        cpu = {"value": cps, "unit": UNIT, "cores": cthreads, "kind": "port",
+               "sample": f"whole workload ({SEQS_PER_GPU}x{SEQ_LEN} tokens), one pass "
+                         f"({csec:.2f} s)"}
+
+    if rank == 0:
+        workload = workload_desc(nseq)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded SplitMix64/Box-Muller, benchmark distributions)",
+            "config": {"workload": workload, "tokens_per_step": T,
+                       "sequences": nseq, "seq_len": SEQ_LEN,
+                       "parallelism": f"head-parallel tp{world}" + (" + nccl all-reduce" if world > 1 else ""),
+                       "l2": "inputs larger than L2 (q,k,v,z = %.0f MB per step)" %
+                             (sum(v.numel() * v.element_size() for n, v in t.items()
+                                  if n in ("q", "k", "v", "z")) / 1e6)},
+            "roofline": roofline,
+            "components": comps,
+            "cpu_baseline": cpu,
+            "e2e": {"value": T / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": 4 * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -295,3 +295,329 @@ def bf16_bits(t) -> np.ndarray:
     """torch bf16 tensor -> numpy uint16 bit patterns (host)."""
     import torch
     return t.detach().to("cpu").contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+# ------------------------------------------------------------ provider --
+# ctypes mirror of include/statecentric_qwen38_provider_api_v1.h.
+
+ABI_V1 = 1
+SCALAR_BF16, SCALAR_F32 = 1, 2
+MEMORY_DEVICE = 1
+STAGE_GDN = 1
+EVENT_PENDING, EVENT_COMPLETE = 0, 1
+GDN_FORWARD_V1 = 1 << 0
+GDN_PREFILL_SPLIT_V2 = 1 << 1
+GDN_PREFILL_SPLIT_V3 = 1 << 2
+GDN_PREFILL_STRIDED_QKV_V4 = 1 << 3
+GDN_PREFILL_POST_CONV_PACK_V5 = 1 << 4
+GDN_POST_PROJECTION_V6 = 1 << 5
+GDN_OUTPUT_TAIL_V7 = 1 << 6
+MAX_RANK = 8
+
+_c = ctypes
+
+
+class HostV1(_c.Structure):
+    _fields_ = [("size", _c.c_uint32), ("abi_version", _c.c_uint32), ("context", _c.c_void_p),
+                ("monotonic_time_ns", _c.CFUNCTYPE(_c.c_uint64, _c.c_void_p))]
+
+
+class CreateV1(_c.Structure):
+    _fields_ = [("size", _c.c_uint32), ("abi_version", _c.c_uint32), ("world_size", _c.c_uint32),
+                ("rank", _c.c_uint32), ("device_ordinal", _c.c_int32),
+                ("assembly_fingerprint_length", _c.c_uint32),
+                ("assembly_fingerprint_sha256", _c.POINTER(_c.c_uint8)),
+                ("configuration", _c.c_void_p), ("configuration_length", _c.c_uint64)]
+
+
+class GdnCreateConfigV1(_c.Structure):
+    _fields_ = [(n, _c.c_uint32) for n in (
+        "size", "abi_version", "hidden_size", "qkv_size_per_rank", "value_size_per_rank",
+        "gate_heads_per_rank", "query_heads_per_rank", "value_heads_per_rank", "head_dim",
+        "max_tokens_per_submission", "prefill_qkv_split_variant", "reserved")]
+
+
+class TensorV1(_c.Structure):
+    _fields_ = [("size", _c.c_uint32), ("abi_version", _c.c_uint32), ("data", _c.c_uint64),
+                ("scalar_type", _c.c_uint32), ("memory_kind", _c.c_uint32),
+                ("device_ordinal", _c.c_int32), ("rank", _c.c_uint32),
+                ("dimensions", _c.c_uint64 * MAX_RANK), ("strides", _c.c_int64 * MAX_RANK),
+                ("byte_length", _c.c_uint64)]
+
+
+class StateRegionV1(_c.Structure):
+    _fields_ = [("size", _c.c_uint32), ("abi_version", _c.c_uint32), ("layer_index", _c.c_uint32),
+                ("reserved", _c.c_uint32), ("state_kind", _c.c_char_p), ("tensor", TensorV1)]
+
+
+class ExecutionV1(_c.Structure):
+    _fields_ = [("size", _c.c_uint32), ("abi_version", _c.c_uint32), ("rank", _c.c_uint32),
+                ("world_size", _c.c_uint32), ("device_ordinal", _c.c_int32),
+                ("stage", _c.c_uint32), ("flags", _c.c_uint32), ("layer_index", _c.c_uint32),
+                ("token_count", _c.c_uint64), ("context_tokens", _c.c_uint64),
+                ("stream", _c.c_uint64), ("input_count", _c.c_uint32),
+                ("output_count", _c.c_uint32), ("inputs", _c.POINTER(TensorV1)),
+                ("outputs", _c.POINTER(TensorV1)), ("mutable_state_count", _c.c_uint32),
+                ("reserved", _c.c_uint32), ("mutable_state", _c.POINTER(StateRegionV1)),
+                ("workspace", _c.c_uint64), ("workspace_length", _c.c_uint64)]
+
+
+class GdnBatchV1(_c.Structure):
+    _fields_ = [("size", _c.c_uint32), ("abi_version", _c.c_uint32), ("state_count", _c.c_uint64),
+                ("reserved", _c.c_uint32), ("reserved1", _c.c_uint32),
+                ("token_offsets", _c.POINTER(_c.c_uint32)),
+                ("token_counts", _c.POINTER(_c.c_uint32))]
+
+
+class ErrorV1(_c.Structure):
+    _fields_ = [("size", _c.c_uint32), ("abi_version", _c.c_uint32), ("status", _c.c_int32),
+                ("reserved", _c.c_uint32), ("message", _c.c_char_p),
+                ("reserved_pointer", _c.c_void_p)]
+
+
+class CompletionV1(_c.Structure):
+    _fields_ = [("size", _c.c_uint32), ("abi_version", _c.c_uint32), ("phase", _c.c_uint32),
+                ("reserved", _c.c_uint32), ("elapsed_ns", _c.c_uint64),
+                ("completed_ns", _c.c_uint64)]
+
+
+_ErrPP = _c.POINTER(_c.POINTER(ErrorV1))
+
+
+class DescriptorV1(_c.Structure):
+    _fields_ = [("size", _c.c_uint32), ("abi_version", _c.c_uint32),
+                ("provider_id", _c.c_char_p), ("provider_version", _c.c_char_p),
+                ("operator_name", _c.c_char_p), ("operator_version", _c.c_uint32),
+                ("stage", _c.c_uint32), ("flags", _c.c_uint32), ("reserved_flags", _c.c_uint32),
+                ("create", _c.CFUNCTYPE(_c.c_int32, _c.POINTER(HostV1), _c.POINTER(CreateV1),
+                                        _c.POINTER(_c.c_void_p), _ErrPP)),
+                ("destroy", _c.CFUNCTYPE(None, _c.c_void_p)),
+                ("submit", _c.CFUNCTYPE(_c.c_int32, _c.c_void_p, _c.POINTER(ExecutionV1),
+                                        _c.c_uint64, _c.POINTER(_c.c_void_p), _ErrPP)),
+                ("poll", _c.CFUNCTYPE(_c.c_int32, _c.c_void_p, _c.c_void_p,
+                                      _c.POINTER(CompletionV1), _ErrPP)),
+                ("wait", _c.CFUNCTYPE(_c.c_int32, _c.c_void_p, _c.c_void_p, _c.c_uint64,
+                                      _c.POINTER(CompletionV1), _ErrPP)),
+                ("cancel", _c.CFUNCTYPE(_c.c_int32, _c.c_void_p, _c.c_void_p, _ErrPP)),
+                ("release_event", _c.CFUNCTYPE(None, _c.c_void_p, _c.c_void_p)),
+                ("release_error", _c.CFUNCTYPE(None, _c.POINTER(ErrorV1))),
+                ("reserved0", _c.c_void_p), ("reserved1", _c.c_void_p),
+                ("reserved2", _c.c_void_p)]
+
+
+def query_descriptor(abi_version=ABI_V1, size=None):
+    """Calls statecentric_qwen38_provider_query_v1; returns (status, descriptor, message)."""
+    L = lib()
+    fn = L.statecentric_qwen38_provider_query_v1
+    fn.argtypes = [_c.c_uint32, _c.c_uint32, _c.POINTER(DescriptorV1), _ErrPP]
+    fn.restype = _c.c_int32
+    d = DescriptorV1()
+    err = _c.POINTER(ErrorV1)()
+    st = fn(abi_version, _c.sizeof(DescriptorV1) if size is None else size, _c.byref(d),
+            _c.byref(err))
+    msg = ""
+    if st != OK and err:
+        msg = err.contents.message.decode()
+        if d.release_error:
+            d.release_error(err)
+    return st, d, msg
+
+
+def tensor_view(t, dims=None, strides=None, device=0) -> TensorV1:
+    """TensorV1 describing torch tensor ``t`` (dims/strides in elements)."""
+    import torch
+    dims = list(t.shape) if dims is None else list(dims)
+    strides = list(t.stride()) if strides is None else list(strides)
+    v = TensorV1()
+    v.size = _c.sizeof(TensorV1)
+    v.abi_version = ABI_V1
+    v.data = t.data_ptr()
+    v.scalar_type = SCALAR_BF16 if t.dtype == torch.bfloat16 else SCALAR_F32
+    v.memory_kind = MEMORY_DEVICE
+    v.device_ordinal = device
+    v.rank = len(dims)
+    for i, (d, s) in enumerate(zip(dims, strides)):
+        v.dimensions[i] = d
+        v.strides[i] = s
+    n = 1
+    for d in dims:
+        n *= d
+    v.byte_length = n * t.element_size()
+    return v
+
+
+class ProviderError(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"provider status {status}: {message}")
+        self.status = status
+
+
+class Provider:
+    """Drives the library only through the descriptor's function pointers,
+    the way a host engine that dlopen()s the provider does."""
+
+    def __init__(self, geom: Geometry, max_tokens: int, world_size=1, rank=0, device=0,
+                 fingerprint=bytes(32)):
+        import time as _time
+        st, d, msg = query_descriptor()
+        if st != OK:
+            raise ProviderError(st, msg)
+        self.d = d
+        self.geom = geom
+        self.device = device
+        self.rank = rank
+        self.world_size = world_size
+        self._clock = HostV1._fields_[3][1](lambda ctx: _time.monotonic_ns())
+        self.host = HostV1(_c.sizeof(HostV1), ABI_V1, None, self._clock)
+        cfg = GdnCreateConfigV1()
+        cfg.size = _c.sizeof(cfg)
+        cfg.abi_version = ABI_V1
+        cfg.hidden_size = geom.hidden
+        cfg.qkv_size_per_rank = 2 * geom.qk_heads * HEAD_DIM + geom.value
+        cfg.value_size_per_rank = geom.value
+        cfg.gate_heads_per_rank = geom.value_heads
+        cfg.query_heads_per_rank = geom.qk_heads
+        cfg.value_heads_per_rank = geom.value_heads
+        cfg.head_dim = HEAD_DIM
+        cfg.max_tokens_per_submission = max_tokens
+        self.cfg = cfg
+        self.fp = (_c.c_uint8 * 32)(*fingerprint[:32])
+        cr = CreateV1(_c.sizeof(CreateV1), ABI_V1, world_size, rank, device, 32,
+                      _c.cast(self.fp, _c.POINTER(_c.c_uint8)), _c.cast(_c.byref(cfg), _c.c_void_p),
+                      _c.sizeof(cfg))
+        self.create_args = cr
+        self.handle = _c.c_void_p()
+        err = _c.POINTER(ErrorV1)()
+        st = d.create(_c.byref(self.host), _c.byref(cr), _c.byref(self.handle), _c.byref(err))
+        self._raise(st, err)
+        self._keep = []
+
+    def _raise(self, st, err):
+        if st != OK:
+            msg = ""
+            if err:
+                msg = err.contents.message.decode()
+                self.d.release_error(err)
+            raise ProviderError(st, msg)
+
+    def _execution(self, flags, inputs, output, states, tokens, stream, batch=None):
+        ins = (TensorV1 * len(inputs))(*inputs)
+        outs = (TensorV1 * 1)(output)
+        st = (StateRegionV1 * max(len(states), 1))(*states) if states else None
+        ex = ExecutionV1()
+        ex.size = _c.sizeof(ex)
+        ex.abi_version = ABI_V1
+        ex.rank = self.rank
+        ex.world_size = self.world_size
+        ex.device_ordinal = self.device
+        ex.stage = STAGE_GDN
+        ex.flags = flags
+        ex.layer_index = 0
+        ex.token_count = tokens
+        ex.stream = stream
+        ex.input_count = len(inputs)
+        ex.output_count = 1
+        ex.inputs = _c.cast(ins, _c.POINTER(TensorV1))
+        ex.outputs = _c.cast(outs, _c.POINTER(TensorV1))
+        ex.mutable_state_count = len(states)
+        ex.mutable_state = _c.cast(st, _c.POINTER(StateRegionV1)) if st is not None else None
+        if batch is not None:
+            ex.workspace = _c.addressof(batch)
+            ex.workspace_length = _c.sizeof(batch)
+        self._keep.append((ins, outs, st, batch))
+        return ex
+
+    @staticmethod
+    def batch_metadata(cu_seqlens):
+        cu = [int(x) for x in cu_seqlens]
+        n = len(cu) - 1
+        offs = (_c.c_uint32 * n)(*cu[:-1])
+        cnts = (_c.c_uint32 * n)(*[cu[i + 1] - cu[i] for i in range(n)])
+        b = GdnBatchV1(_c.sizeof(GdnBatchV1), ABI_V1, n, 0, 0,
+                       _c.cast(offs, _c.POINTER(_c.c_uint32)),
+                       _c.cast(cnts, _c.POINTER(_c.c_uint32)))
+        b._arrays = (offs, cnts)
+        return b
+
+    def submit_layer(self, t, state, out, cu_seqlens, stream=None, deadline_s=60.0,
+                     conv_state=None):
+        """Post-projection GDN layer (GDN_FORWARD_V1 | GDN_POST_PROJECTION_V6).
+        ``t`` holds q, k, v, a, b, z, A_log, dt_bias, gamma, w_out as torch tensors."""
+        import time as _time
+        g = self.geom
+        T = t["q"].shape[0]
+        D = HEAD_DIM
+        dv = self.device
+        inputs = [
+            tensor_view(t["q"], [T, g.qk_heads * D], [g.qk_heads * D, 1], dv),
+            tensor_view(t["k"], [T, g.qk_heads * D], [g.qk_heads * D, 1], dv),
+            tensor_view(t["v"], [T, g.value], [g.value, 1], dv),
+            tensor_view(t["a"], [T, g.value_heads], [g.value_heads, 1], dv),
+            tensor_view(t["b"], [T, g.value_heads], [g.value_heads, 1], dv),
+            tensor_view(t["z"], [T, g.value], [g.value, 1], dv),
+            tensor_view(t["A_log"], [g.value_heads], [1], dv),
+            tensor_view(t["dt_bias"], [g.value_heads], [1], dv),
+            tensor_view(t["gamma"], [D], [1], dv),
+            tensor_view(t["w_out"], [g.value, g.hidden], [1, g.value], dv),
+        ]
+        S = state.shape[0]
+        rs = StateRegionV1(_c.sizeof(StateRegionV1), ABI_V1, 0, 0, b"gdn.recurrent",
+                           tensor_view(state, device=dv))
+        states = [rs]
+        if conv_state is not None:
+            states = [StateRegionV1(_c.sizeof(StateRegionV1), ABI_V1, 0, 0, b"gdn.conv",
+                                    tensor_view(conv_state, device=dv)), rs]
+        batch = self.batch_metadata(cu_seqlens) if S > 1 else None
+        ex = self._execution(GDN_FORWARD_V1 | GDN_POST_PROJECTION_V6, inputs,
+                             tensor_view(out, device=dv), states, T,
+                             _stream(stream).value or 0, batch)
+        return self.submit(ex, deadline_s)
+
+    def submit_tail(self, o, z, gamma, w_out, out, stream=None, deadline_s=60.0):
+        g = self.geom
+        rows = o.shape[0]
+        dv = self.device
+        inputs = [tensor_view(o, [rows, g.value], [g.value, 1], dv),
+                  tensor_view(z, [rows, g.value], [g.value, 1], dv),
+                  tensor_view(gamma, [HEAD_DIM], [1], dv),
+                  tensor_view(w_out, [g.value, g.hidden], [1, g.value], dv)]
+        ex = self._execution(GDN_FORWARD_V1 | GDN_OUTPUT_TAIL_V7, inputs,
+                             tensor_view(out, device=dv), [], rows, _stream(stream).value or 0)
+        return self.submit(ex, deadline_s)
+
+    def submit(self, ex, deadline_s=60.0, deadline_ns=None):
+        import time as _time
+        if deadline_ns is None:
+            deadline_ns = _time.monotonic_ns() + int(deadline_s * 1e9)
+        ev = _c.c_void_p()
+        err = _c.POINTER(ErrorV1)()
+        st = self.d.submit(self.handle, _c.byref(ex), deadline_ns, _c.byref(ev), _c.byref(err))
+        self._keep.clear()
+        self._raise(st, err)
+        return ev
+
+    def wait(self, ev, timeout_s=60.0):
+        import time as _time
+        c = CompletionV1()
+        err = _c.POINTER(ErrorV1)()
+        st = self.d.wait(self.handle, ev, _time.monotonic_ns() + int(timeout_s * 1e9),
+                         _c.byref(c), _c.byref(err))
+        self._raise(st, err)
+        return c
+
+    def poll(self, ev):
+        c = CompletionV1()
+        err = _c.POINTER(ErrorV1)()
+        st = self.d.poll(self.handle, ev, _c.byref(c), _c.byref(err))
+        if st == NOT_READY:
+            return None
+        self._raise(st, err)
+        return c
+
+    def release(self, ev):
+        self.d.release_event(self.handle, ev)
+
+    def close(self):
+        if self.handle:
+            self.d.destroy(self.handle)
+            self.handle = _c.c_void_p()
