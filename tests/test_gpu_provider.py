@@ -84,10 +84,20 @@ def test_provider_rejections(setup, cuda):
     # Null stream (the reference requires a stream too).
     _expect(G.INVALID_ARGUMENT,
             lambda: prov.submit_layer(base, st, out, cu, stream=torch.cuda.default_stream()))
-    # Wrong v geometry.
-    bad = dict(base, v=base["v"][:, :16].contiguous())
-    _expect(G.INVALID_ARGUMENT, lambda: prov.submit_layer(bad, st, out, cu, stream=stream),
-            "geometry")
+    # Wrong v geometry, wrong dtype, wrong state kind.
+    def narrow_v(ins, rs):
+        ins[2].dimensions[1] = GEOM.value // 2
+        ins[2].byte_length //= 2
+
+    def f32_gamma(ins, rs):
+        ins[8].scalar_type = G.SCALAR_F32
+
+    def conv_kind(ins, rs):
+        rs.state_kind = b"gdn.conv"
+
+    for mutate in (narrow_v, f32_gamma, conv_kind):
+        _expect(G.INVALID_ARGUMENT,
+                lambda: _submit_raw(prov, base, st, out, cu, stream, mutate=mutate), "geometry")
     # Ranges not packed / not covering the tokens.
     _expect(G.INVALID_ARGUMENT,
             lambda: _submit_raw(prov, base, st, out, [0, 64, 128], stream, offsets=[0, 63]),
@@ -107,7 +117,7 @@ def test_provider_rejections(setup, cuda):
 
 
 def _submit_raw(prov, t, state, out, cu, stream, offsets=None, counts=None, flags=None,
-                layer=0):
+                layer=0, mutate=None):
     """Builds an execution by hand to reach the individual validation clauses."""
     batch = G.Provider.batch_metadata(cu)
     if offsets is not None:
@@ -129,6 +139,8 @@ def _submit_raw(prov, t, state, out, cu, stream, offsets=None, counts=None, flag
            G.tensor_view(t["w_out"], [g.value, g.hidden], [1, g.value])]
     rs = G.StateRegionV1(ctypes.sizeof(G.StateRegionV1), 1, layer, 0, b"gdn.recurrent",
                          G.tensor_view(state))
+    if mutate is not None:
+        mutate(ins, rs)
     ex = prov._execution(flags if flags is not None else (G.GDN_FORWARD_V1 | G.GDN_POST_PROJECTION_V6),
                          ins, G.tensor_view(out), [rs], T, stream.cuda_stream, batch)
     ex.layer_index = layer
