@@ -72,6 +72,27 @@ GDN_B200_API int32_t gdn_b200_output_tail(const void* o, const void* z, const vo
                              void* workspace, uint64_t workspace_bytes,
                              void* stream);
 
+/* Output tail that allocates nothing and takes no workspace: for callers that
+ * cannot provide device scratch (an operator interface that passes only
+ * inputs and outputs, or a serving loop bound to a memory plan frozen at
+ * start-up, where cudaMalloc is not allowed).  This entry point has no
+ * counterpart in the reference.  Its scratch is a static device array of
+ * GDN_B200_NO_ALLOC_SCRATCH_BYTES held by every GPU that loads the library;
+ * sizes are limited to rows <= 128, value_heads * 128 <= 4096, hidden <= 2048
+ * (larger sizes return INVALID_ARGUMENT).  All calls on a device share the
+ * array: calls that overlap on the GPU race and must be serialised.  The
+ * first call on a device resolves the array's device address; make it before
+ * any stream capture. */
+#define GDN_B200_NO_ALLOC_MAX_ROWS 128
+#define GDN_B200_NO_ALLOC_MAX_VALUE 4096
+#define GDN_B200_NO_ALLOC_MAX_HIDDEN 2048
+#define GDN_B200_NO_ALLOC_SCRATCH_BYTES (256ull + 128ull * 4096ull * 2ull + 16ull * 128ull * 2048ull * 4ull)
+GDN_B200_API int32_t gdn_b200_output_tail_no_alloc(const void* o, const void* z,
+                                                   const void* gamma, const void* w_out,
+                                                   void* out, int64_t rows,
+                                                   int32_t value_heads, int32_t hidden,
+                                                   float eps, void* stream);
+
 /* One decode step for `batch` sequences of one token each: gating, q/k
  * L2-norm, S <- exp(g) S; S += beta k (v - S^T k)^T; o = scale S^T q,
  * scale = 128^-1/2.  Replaces PackedDecodeRecurrentV12 (P:1308-1369) with the
