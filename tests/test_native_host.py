@@ -69,12 +69,14 @@ def test_provider_abi_layout_matches_python_mirror(tmp_path):
 def test_library_exports_every_declared_symbol():
     out = subprocess.run(["nm", "-D", "--defined-only", G.LIB_PATH], capture_output=True,
                          text=True, check=True).stdout
+    import re
     exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
     declared = set()
     for header in ("gdn_b200.h", "statecentric_qwen38_provider_api_v1.h"):
         text = open(os.path.join(INCLUDE, header)).read()
-        for name in G.EXPORTED_SYMBOLS:
-            if name + "(" in text.replace(" (", "("):
-                declared.add(name)
-    assert declared == set(G.EXPORTED_SYMBOLS)
+        declared |= set(re.findall(r"GDN_B200_API\s+[\w\s\*]+?\b(gdn_b200_\w+)\s*\(", text))
+        declared |= set(re.findall(r"\b(statecentric_qwen38_provider_query_v1)\s*\(", text))
+    assert set(G.EXPORTED_SYMBOLS) <= declared
     assert declared <= exported, declared - exported
+    for name in declared:
+        getattr(G.lib(), name)
