@@ -69,12 +69,72 @@ __device__ __forceinline__ void group_barrier(int id, int threads) {
 
 // ============================================================ prep =====
 
+// Block row I of T = (I + A)^-1 (16x16 blocks, diagonal blocks already in T):
+// T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ for every J < I at once.  T's
+// strictly upper blocks are zero, so the inner sum runs over m in [0, 16 I)
+// for every column and all trip counts are compile-time constants.
+// Thread u -> column cc = u % (16 I) and rows r0 + k * rstep.
+template <int I>
+__device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], float (*X)[52],
+                                                int u, int grp, bool live) {
+  constexpr int kCols = 16 * I;
+  constexpr int kStep = 128 / kCols;              // 8, 4, 2
+  constexpr int kRows = (16 + kStep - 1) / kStep; // 2, 4, 8
+  const int cc = u % kCols;
+  const int r0 = u / kCols;
+  const bool worker = live && r0 < kStep;
+  float acc[kRows];
+  if (worker) {
+    float tcol[kCols];
+#pragma unroll
+    for (int m = 0; m < kCols; ++m) tcol[m] = T[m][cc];
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) {
+      const int rr = r0 + k * kStep;
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int m = 0; m < kCols; m += 4) {
+        const float4 av = *reinterpret_cast<const float4*>(&A[16 * I + rr][m]);
+        a0 += av.x * tcol[m] + av.y * tcol[m + 1];
+        a1 += av.z * tcol[m + 2] + av.w * tcol[m + 3];
+      }
+      acc[k] = a0 + a1;
+    }
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) X[r0 + k * kStep][cc] = acc[k];
+  }
+  group_barrier(1 + grp, 128);
+  if (worker) {
+    float xcol[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) xcol[m] = X[m][cc];
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) {
+      const int rr = r0 + k * kStep;
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; m += 4) {
+        const float4 tv = *reinterpret_cast<const float4*>(&T[16 * I + rr][16 * I + m]);
+        a0 += tv.x * xcol[m] + tv.y * xcol[m + 1];
+        a1 += tv.z * xcol[m + 2] + tv.w * xcol[m + 3];
+      }
+      acc[k] = -(a0 + a1);
+    }
+  }
+  group_barrier(1 + grp, 128);
+  if (worker) {
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) T[16 * I + r0 + k * kStep][cc] = acc[k];
+  }
+  group_barrier(1 + grp, 128);
+}
+
+
 constexpr int kPrepThreads = 256;
 
 struct PrepSmem {
   uint8_t kq[kKQBytes];     // [K;Q] operand tile (1024-aligned)
-  float amat[2][64][68];    // A of the two v-heads in flight (row stride 68)
-  float tmat[2][64][68];    // T = (I + A)^-1
+  float amat[2][64][68];    // A, overwritten in place by T = (I + A)^-1
   float xs[2][16][52];      // block-merge temporaries
   float g[2][64];           // cumsum G
   float e1[2][64];          // exp(g_t) = exp(G_t - G_{t-1})
@@ -114,11 +174,15 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
   if (warp == 0) tmem_alloc(&sm.tmem, 64);
 
   // Gate inputs of the first v-head pair, fetched before the long q/k loads.
-  float pre_a = 0.f, pre_b = 0.f;
-  if (grp < group && u < n) {
-    const int64_t gi = static_cast<int64_t>(t0 + u) * value_heads + kh * group + grp;
-    pre_a = bf16_bits_to_f32(a[gi]);
-    pre_b = bf16_bits_to_f32(b[gi]);
+  float pre_a = 0.f, pre_b = 0.f, pre_alog = 0.f, pre_dt = 0.f;
+  if (grp < group && u < 64) {
+    pre_alog = A_log[kh * group + grp];
+    pre_dt = dt_bias[kh * group + grp];
+    if (u < n) {
+      const int64_t gi = static_cast<int64_t>(t0 + u) * value_heads + kh * group + grp;
+      pre_a = bf16_bits_to_f32(a[gi]);
+      pre_b = bf16_bits_to_f32(b[gi]);
+    }
   }
 
   // q/k rows -> RmsNorm L2-norm (gamma bf16(1/sqrt(128)), eps 1e-6/128) ->
@@ -183,8 +247,10 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
 
   bool ok = true;
   bool waited = false;
+  // T overwrites A in place: block row I of A is last read while block row
+  // I of T is formed, and T's strictly upper part equals A's (zero).
   float (*A)[68] = sm.amat[grp];
-  float (*T)[68] = sm.tmat[grp];
+  float (*T)[68] = sm.amat[grp];
   float (*X)[52] = sm.xs[grp];
 
   for (int hp = 0; hp < group; hp += 2) {
@@ -197,15 +263,19 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
     // Gating (aclnnFusedGdnGating: softplus beta 1, threshold 20) and the
     // in-chunk cumsum as two warp scans.
     if (active && u < 64) {
-      float ga = pre_a, gb = pre_b;
-      if (hp > 0 && u < n) {
-        const int64_t gi = static_cast<int64_t>(t0 + u) * value_heads + h;
-        ga = bf16_bits_to_f32(a[gi]);
-        gb = bf16_bits_to_f32(b[gi]);
+      float ga = pre_a, gb = pre_b, alog = pre_alog, dtb = pre_dt;
+      if (hp > 0) {
+        alog = A_log[h];
+        dtb = dt_bias[h];
+        if (u < n) {
+          const int64_t gi = static_cast<int64_t>(t0 + u) * value_heads + h;
+          ga = bf16_bits_to_f32(a[gi]);
+          gb = bf16_bits_to_f32(b[gi]);
+        }
       }
       float g = 0.f, bt = 0.f;
       if (u < n) {
-        g = -expf(A_log[h]) * softplus20(ga + dt_bias[h]);
+        g = -expf(alog) * softplus20(ga + dtb);
         bt = round_bf16(1.0f / (1.0f + expf(-gb)));
       }
       sm.e1[grp][u] = __expf(g);
@@ -217,11 +287,6 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
       if (u == 31) sm.carry[grp] = g;
       sm.beta[grp][u] = bt;
       sm.g[grp][u] = g;
-    }
-    // T starts as zero (its strictly upper blocks stay zero).
-    for (int e = u; e < 64 * 16; e += 128) {
-      const int i = e >> 4, c4 = (e & 15) * 4;
-      *reinterpret_cast<float4*>(&T[i][c4]) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     group_barrier(1 + grp, 128);
     if (active && u >= 32 && u < 64) sm.g[grp][u] += sm.carry[grp];
@@ -255,12 +320,29 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
       if (u < 64) {
         // Lane u holds row u of K K^T = column u (symmetric).  Column u of A:
         // A[i][u] = beta_i KK_iu exp(G_i - G_u) for u < i < n, with the decay
-        // formed as a running product of the per-token exp(g).
+        // formed as a running product of the per-token exp(g).  The factors
+        // are read into registers first so the loop carries no shared-memory
+        // loads behind the stores to A.
         float d = 1.f;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          d = (i > u) ? d * sm.e1[grp][i] : 1.f;
-          A[i][u] = (i > u && i < n) ? sm.beta[grp][i] * __uint_as_float(r[i]) * d : 0.f;
+        for (int c = 0; c < 64; c += 16) {
+          float e1v[16], bv[16];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 ev = *reinterpret_cast<const float4*>(&sm.e1[grp][c + 4 * q4]);
+            const float4 bb = *reinterpret_cast<const float4*>(&sm.beta[grp][c + 4 * q4]);
+            e1v[4 * q4] = ev.x; e1v[4 * q4 + 1] = ev.y; e1v[4 * q4 + 2] = ev.z; e1v[4 * q4 + 3] = ev.w;
+            bv[4 * q4] = bb.x; bv[4 * q4 + 1] = bb.y; bv[4 * q4 + 2] = bb.z; bv[4 * q4 + 3] = bb.w;
+          }
+          float col[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int i = c + j;
+            d = (i > u) ? d * e1v[j] : 1.f;
+            col[j] = (i > u && i < n) ? bv[j] * __uint_as_float(r[i]) * d : 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) A[c + j][u] = col[j];
         }
       } else {
         // Lane 64+i holds row i of Q K^T: P[i][j] = QK_ij exp(G_i - G_j),
@@ -269,11 +351,21 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
         float d = 1.f;
         uint32_t w[32];
 #pragma unroll
-        for (int j = 63; j >= 0; --j) {
-          const float pj = (j <= i && i < n) ? __uint_as_float(r[j]) * d : 0.f;
-          d = (j <= i) ? d * sm.e1[grp][j] : 1.f;
-          if (j & 1) w[j >> 1] = __float_as_uint(pj);
-          else w[j >> 1] = pack_bf16x2(pj, __uint_as_float(w[j >> 1]));
+        for (int c = 48; c >= 0; c -= 16) {
+          float e1v[16];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 ev = *reinterpret_cast<const float4*>(&sm.e1[grp][c + 4 * q4]);
+            e1v[4 * q4] = ev.x; e1v[4 * q4 + 1] = ev.y; e1v[4 * q4 + 2] = ev.z; e1v[4 * q4 + 3] = ev.w;
+          }
+#pragma unroll
+          for (int jj = 15; jj >= 0; --jj) {
+            const int j = c + jj;
+            const float pj = (j <= i && i < n) ? __uint_as_float(r[j]) * d : 0.f;
+            d = (j <= i) ? d * e1v[jj] : 1.f;
+            if (j & 1) w[j >> 1] = __float_as_uint(pj);
+            else w[j >> 1] = pack_bf16x2(pj, __uint_as_float(w[j >> 1]));
+          }
         }
 #pragma unroll
         for (int c = 0; c < 8; ++c)
@@ -286,61 +378,27 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
     // T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution
     // (one thread per block column), then block rows I = 1..3:
     //   T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ.
-    if (active && ok && u < 64) {
-      const int bl = u >> 4, c = u & 15, o = bl * 16;
-      float x[16];
+    const bool diag = active && ok && u < 64;
+    const int bl = u >> 4, dc = u & 15, o = bl * 16;
+    float x[16];
+    if (diag) {
 #pragma unroll
       for (int rr = 0; rr < 16; ++rr) {
-        float acc = (rr == c) ? 1.f : 0.f;
+        float acc = (rr == dc) ? 1.f : 0.f;
 #pragma unroll
         for (int m = 0; m < rr; ++m) acc -= A[o + rr][o + m] * x[m];
         x[rr] = acc;
       }
+    }
+    group_barrier(1 + grp, 128);  // every read of the diagonal A blocks is done
+    if (diag) {
 #pragma unroll
-      for (int rr = 0; rr < 16; ++rr) T[o + rr][o + c] = x[rr];
+      for (int rr = 0; rr < 16; ++rr) T[o + rr][o + dc] = x[rr];
     }
     group_barrier(1 + grp, 128);
-#pragma unroll
-    for (int I = 1; I < 4; ++I) {
-      // X[r][cc] = sum_{m=16J}^{16I-1} A[16I+r][m] T[m][cc], cc < 16I; each
-      // thread does I column pairs of one row.
-      if (active && ok) {
-#pragma unroll
-        for (int s = 0; s < I; ++s) {
-          const int e = u + 128 * s;           // pair index < 128 I
-          const int rr = e / (8 * I);
-          const int cc = (e % (8 * I)) * 2;
-          const int J = cc >> 4;
-          float x0 = 0.f, x1 = 0.f;
-          for (int m = 16 * J; m < 16 * I; ++m) {
-            const float av = A[16 * I + rr][m];
-            const float2 tv = *reinterpret_cast<const float2*>(&T[m][cc]);
-            x0 += av * tv.x;
-            x1 += av * tv.y;
-          }
-          *reinterpret_cast<float2*>(&X[rr][cc]) = make_float2(x0, x1);
-        }
-      }
-      group_barrier(1 + grp, 128);
-      if (active && ok) {
-#pragma unroll
-        for (int s = 0; s < I; ++s) {
-          const int e = u + 128 * s;
-          const int rr = e / (8 * I);
-          const int cc = (e % (8 * I)) * 2;
-          float y0 = 0.f, y1 = 0.f;
-#pragma unroll
-          for (int m = 0; m < 16; ++m) {
-            const float tv = T[16 * I + rr][16 * I + m];
-            const float2 xv = *reinterpret_cast<const float2*>(&X[m][cc]);
-            y0 += tv * xv.x;
-            y1 += tv * xv.y;
-          }
-          *reinterpret_cast<float2*>(&T[16 * I + rr][cc]) = make_float2(-y0, -y1);
-        }
-      }
-      group_barrier(1 + grp, 128);
-    }
+    merge_block_row<1>(A, T, X, u, grp, active && ok);
+    merge_block_row<2>(A, T, X, u, grp, active && ok);
+    merge_block_row<3>(A, T, X, u, grp, active && ok);
     // Store T as K-rows j of the MN-major operand image (hi/lo pair):
     // thread -> column j = u / 2, rows [32 (u % 2), +32).
     if (active && ok) {
