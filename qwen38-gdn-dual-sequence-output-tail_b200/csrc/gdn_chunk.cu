@@ -32,6 +32,7 @@
 // The reference's W = T (beta exp(G) K) is never formed:
 // v_new = U - W S = T (beta V - beta exp(G) (K S)) needs one product with T.
 // Decay factors are always exp of a non-positive difference.
+#include <algorithm>
 #include <vector>
 
 #include "gdn_common.cuh"
@@ -133,20 +134,28 @@ __device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], 
 constexpr int kPrepThreads = 256;
 
 struct PrepSmem {
-  uint8_t kq[kKQBytes];     // [K;Q] operand tile (1024-aligned)
+  uint8_t kq[2][kKQBytes];  // [K;Q] tiles of two units (1024-aligned): raw q/k land
+                            // here by TMA and are normalised in place
   float amat[2][64][68];    // A, overwritten in place by T = (I + A)^-1
   float xs[2][16][52];      // block-merge temporaries
   float g[2][64];           // cumsum G
   float e1[2][64];          // exp(g_t) = exp(G_t - G_{t-1})
   float beta[2][64];
   float carry[2];
-  uint64_t bar;
+  uint64_t full[2];         // raw tile of the unit in kq[i] has landed
+  uint64_t mma;             // [K;Q] K^T of the current unit has completed
   uint32_t tmem;
 };
 
-__global__ void __launch_bounds__(kPrepThreads)
-gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __restrict__ q,
-                      const uint16_t* __restrict__ k, const uint16_t* __restrict__ a,
+// Persistent: CTA x handles units x, x + gridDim.x, ... (unit = chunk * Hk +
+// q/k head).  While one unit is processed, the raw q/k tile of the next one
+// is already on its way into the other buffer, and the finished [K;Q] image
+// goes back to global memory as one bulk store.
+__global__ void __launch_bounds__(kPrepThreads, 2)
+gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
+                      const __grid_constant__ CUtensorMap tm_q,
+                      const __grid_constant__ CUtensorMap tm_k,
+                      const uint16_t* __restrict__ a,
                       const uint16_t* __restrict__ b, const float* __restrict__ A_log,
                       const float* __restrict__ dt_bias, uint8_t* __restrict__ kq_records,
                       uint8_t* __restrict__ records, int qk_heads, int value_heads,
@@ -154,12 +163,7 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
   extern __shared__ uint8_t smem_raw[];
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const int chunk = blockIdx.x;
-  const int kh = blockIdx.y;
-  if (chunk >= tab.total_chunks) return;
-  const int seq = find_seq(tab, chunk);
-  const int t0 = tab.cu[seq] + (chunk - tab.chunk_start[seq]) * kChunk;
-  const int n = min(kChunk, tab.cu[seq + 1] - t0);
+  const int units = tab.total_chunks * qk_heads;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int group = value_heads / qk_heads;
@@ -167,256 +171,300 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
   const int u = threadIdx.x & 127;
   const int quarter = warp & 3;         // TMEM lane quarter of this warp
 
+  // Raw q/k tile of a unit: K rows 0-63 and Q rows 64-127 of both 64-column
+  // slabs, four 8 KB boxes (tokens past the tensor read as zero).
+  auto load_unit = [&](int unit, int buf) {
+    const int chunk = unit / qk_heads;
+    const int kh = unit - chunk * qk_heads;
+    const int seq = find_seq(tab, chunk);
+    const int t0 = tab.cu[seq] + (chunk - tab.chunk_start[seq]) * kChunk;
+    uint8_t* dst = sm.kq[buf];
+    mbar_arrive_expect_tx(&sm.full[buf], kKQBytes);
+    tma_load_3d(dst, &tm_k, &sm.full[buf], 0, kh, t0);
+    tma_load_3d(dst + 16384, &tm_k, &sm.full[buf], 64, kh, t0);
+    tma_load_3d(dst + 8192, &tm_q, &sm.full[buf], 0, kh, t0);
+    tma_load_3d(dst + 16384 + 8192, &tm_q, &sm.full[buf], 64, kh, t0);
+  };
+
   if (threadIdx.x == 0) {
-    mbar_init(&sm.bar, 1);
+    mbar_init(&sm.full[0], 1);
+    mbar_init(&sm.full[1], 1);
+    mbar_init(&sm.mma, 1);
     fence_barrier_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    if (static_cast<int>(blockIdx.x) < units) load_unit(blockIdx.x, 0);
   }
   if (warp == 0) tmem_alloc(&sm.tmem, 64);
-
-  // Gate inputs of the first v-head pair, fetched before the long q/k loads.
-  float pre_a = 0.f, pre_b = 0.f, pre_alog = 0.f, pre_dt = 0.f;
-  if (grp < group && u < 64) {
-    pre_alog = A_log[kh * group + grp];
-    pre_dt = dt_bias[kh * group + grp];
-    if (u < n) {
-      const int64_t gi = static_cast<int64_t>(t0 + u) * value_heads + kh * group + grp;
-      pre_a = bf16_bits_to_f32(a[gi]);
-      pre_b = bf16_bits_to_f32(b[gi]);
-    }
-  }
-
-  // q/k rows -> RmsNorm L2-norm (gamma bf16(1/sqrt(128)), eps 1e-6/128) ->
-  // bf16 -> swizzled tile in shared memory and the same bytes to the record.
-  // Two threads per row (row r = tid / 2, half = tid % 2 -> 64 columns =
-  // eight 16-byte chunks, the 64-column slab `half` of the tile); all loads
-  // are issued before any use.
-  uint8_t* kq_rec = kq_records + (static_cast<int64_t>(chunk) * qk_heads + kh) * kKQBytes;
-  {
-    const float l2gamma = round_bf16(0.08838834764831845f);
-    const int r = threadIdx.x >> 1;
-    const int half = threadIdx.x & 1;
-    const int tok = r & 63;
-    const uint4* src = reinterpret_cast<const uint4*>(
-        (r < 64 ? k : q) + (static_cast<int64_t>(t0 + tok) * qk_heads + kh) * kHeadDim + half * 64);
-    uint4 raw[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) raw[c] = (tok < n) ? src[c] : make_uint4(0u, 0u, 0u, 0u);
-    float ss = 0.f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const float x0 = bf16lo_f32(w[p]), x1 = bf16hi_f32(w[p]);
-        ss += x0 * x0 + x1 * x1;
-      }
-    }
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    const float rs = rsqrtf(ss * (1.0f / 128.0f) + 1.0e-6f / 128.0f) * l2gamma;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
-      uint4 o;
-      o.x = pack_bf16x2(bf16lo_f32(w[0]) * rs, bf16hi_f32(w[0]) * rs);
-      o.y = pack_bf16x2(bf16lo_f32(w[1]) * rs, bf16hi_f32(w[1]) * rs);
-      o.z = pack_bf16x2(bf16lo_f32(w[2]) * rs, bf16hi_f32(w[2]) * rs);
-      o.w = pack_bf16x2(bf16lo_f32(w[3]) * rs, bf16hi_f32(w[3]) * rs);
-      const uint32_t off = half * 16384u + sw128_chunk(r, c);
-      *reinterpret_cast<uint4*>(sm.kq + off) = o;
-      *reinterpret_cast<uint4*>(kq_rec + off) = o;
-    }
-  }
-  fence_proxy_async_smem();
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem = sm.tmem;
 
-  // D[128 x 64] = [K;Q] K^T: lanes 0-63 hold K K^T, lanes 64-127 Q K^T.
-  if (threadIdx.x == 0) {
-    constexpr uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
-    const uint32_t t = smem_u32(sm.kq);
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint32_t off = (kk >> 2) * 16384u + (kk & 3) * 32u;
-      umma_bf16(tmem, umma_sdesc(t + off, 16, 1024), umma_sdesc(t + off, 16, 1024), idesc,
-                kk > 0 ? 1u : 0u);
-    }
-    umma_commit(&sm.bar);
-  }
+  int it = 0;
+  for (int unit = blockIdx.x; unit < units; unit += gridDim.x, ++it) {
+    const int buf = it & 1;
+    const int chunk = unit / qk_heads;
+    const int kh = unit - chunk * qk_heads;
+    const int seq = find_seq(tab, chunk);
+    const int t0 = tab.cu[seq] + (chunk - tab.chunk_start[seq]) * kChunk;
+    const int n = min(kChunk, tab.cu[seq + 1] - t0);
 
-  bool ok = true;
-  bool waited = false;
-  // T overwrites A in place: block row I of A is last read while block row
-  // I of T is formed, and T's strictly upper part equals A's (zero).
-  float (*A)[68] = sm.amat[grp];
-  float (*T)[68] = sm.amat[grp];
-  float (*X)[52] = sm.xs[grp];
-
-  for (int hp = 0; hp < group; hp += 2) {
-    const int hl = hp + grp;
-    const bool active = hl < group;
-    const int h = kh * group + (active ? hl : 0);
-    uint8_t* rec = records + (static_cast<int64_t>(chunk) * value_heads + h) * kRecBytes;
-    float* fac = reinterpret_cast<float*>(rec + kRecF);
-
-    // Gating (aclnnFusedGdnGating: softplus beta 1, threshold 20) and the
-    // in-chunk cumsum as two warp scans.
-    if (active && u < 64) {
-      float ga = pre_a, gb = pre_b, alog = pre_alog, dtb = pre_dt;
-      if (hp > 0) {
-        alog = A_log[h];
-        dtb = dt_bias[h];
-        if (u < n) {
-          const int64_t gi = static_cast<int64_t>(t0 + u) * value_heads + h;
-          ga = bf16_bits_to_f32(a[gi]);
-          gb = bf16_bits_to_f32(b[gi]);
-        }
-      }
-      float g = 0.f, bt = 0.f;
+    // Gate inputs of the first v-head pair, fetched before the tile wait.
+    float pre_a = 0.f, pre_b = 0.f, pre_alog = 0.f, pre_dt = 0.f;
+    if (grp < group && u < 64) {
+      pre_alog = A_log[kh * group + grp];
+      pre_dt = dt_bias[kh * group + grp];
       if (u < n) {
-        g = -expf(alog) * softplus20(ga + dtb);
-        bt = round_bf16(1.0f / (1.0f + expf(-gb)));
+        const int64_t gi = static_cast<int64_t>(t0 + u) * value_heads + kh * group + grp;
+        pre_a = bf16_bits_to_f32(a[gi]);
+        pre_b = bf16_bits_to_f32(b[gi]);
       }
-      sm.e1[grp][u] = __expf(g);
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, g, o);
-        if (lane >= o) g += y;
-      }
-      if (u == 31) sm.carry[grp] = g;
-      sm.beta[grp][u] = bt;
-      sm.g[grp][u] = g;
-    }
-    group_barrier(1 + grp, 128);
-    if (active && u >= 32 && u < 64) sm.g[grp][u] += sm.carry[grp];
-    group_barrier(1 + grp, 128);
-    if (active && u < 64) {
-      const float gi = sm.g[grp][u];
-      const float glast = sm.g[grp][n - 1];
-      const float bt = sm.beta[grp][u];
-      const float egi = __expf(gi);
-      fac[kFBeta + u] = bt;
-      fac[kFBetaEG + u] = bt * egi;
-      fac[kFEG + u] = egi;
-      fac[kFED + u] = __expf(glast - gi);
-      if (u == 0) fac[kFELast] = __expf(glast);
     }
 
-    if (!waited) {
-      ok = mbar_wait(&sm.bar, 0, err);
-      waited = true;
+    // q/k rows -> RmsNorm L2-norm (gamma bf16(1/sqrt(128)), eps 1e-6/128) ->
+    // bf16, in place.  Two threads per row (row r = tid / 2, half = tid % 2:
+    // the 64-column slab `half`, eight 16-byte chunks); rows past the chunk
+    // are zeroed.
+    bool landed = mbar_wait(&sm.full[buf], (it >> 1) & 1, err);
+    {
+      uint8_t* tile = sm.kq[buf];
+      const float l2gamma = round_bf16(0.08838834764831845f);
+      const int r = threadIdx.x >> 1;
+      const int half = threadIdx.x & 1;
+      const int tok = r & 63;
+      uint4 raw[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        raw[c] = (landed && tok < n)
+                     ? *reinterpret_cast<const uint4*>(tile + half * 16384u + sw128_chunk(r, c))
+                     : make_uint4(0u, 0u, 0u, 0u);
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float x0 = bf16lo_f32(w[p]), x1 = bf16hi_f32(w[p]);
+          ss += x0 * x0 + x1 * x1;
+        }
+      }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      const float rs = rsqrtf(ss * (1.0f / 128.0f) + 1.0e-6f / 128.0f) * l2gamma;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+        uint4 o;
+        o.x = pack_bf16x2(bf16lo_f32(w[0]) * rs, bf16hi_f32(w[0]) * rs);
+        o.y = pack_bf16x2(bf16lo_f32(w[1]) * rs, bf16hi_f32(w[1]) * rs);
+        o.z = pack_bf16x2(bf16lo_f32(w[2]) * rs, bf16hi_f32(w[2]) * rs);
+        o.w = pack_bf16x2(bf16lo_f32(w[3]) * rs, bf16hi_f32(w[3]) * rs);
+        *reinterpret_cast<uint4*>(tile + half * 16384u + sw128_chunk(r, c)) = o;
+      }
     }
+    fence_proxy_async_smem();
+    tmem_fence_before();
+    __syncthreads();
     tmem_fence_after();
-    if (active && ok) {
-      const uint32_t base = tmem_addr(tmem, quarter * 32, 0);
-      uint32_t r[64];
-#pragma unroll
-      for (int c = 0; c < 64; c += 16) {
-        uint32_t* rc = r + c;
-        tmem_ld16(base + c, *reinterpret_cast<uint32_t(*)[16]>(rc));
-      }
-      tmem_ld_wait();
-      if (u < 64) {
-        // Lane u holds row u of K K^T = column u (symmetric).  Column u of A:
-        // A[i][u] = beta_i KK_iu exp(G_i - G_u) for u < i < n, with the decay
-        // formed as a running product of the per-token exp(g).  The factors
-        // are read into registers first so the loop carries no shared-memory
-        // loads behind the stores to A.
-        float d = 1.f;
-#pragma unroll
-        for (int c = 0; c < 64; c += 16) {
-          float e1v[16], bv[16];
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const float4 ev = *reinterpret_cast<const float4*>(&sm.e1[grp][c + 4 * q4]);
-            const float4 bb = *reinterpret_cast<const float4*>(&sm.beta[grp][c + 4 * q4]);
-            e1v[4 * q4] = ev.x; e1v[4 * q4 + 1] = ev.y; e1v[4 * q4 + 2] = ev.z; e1v[4 * q4 + 3] = ev.w;
-            bv[4 * q4] = bb.x; bv[4 * q4 + 1] = bb.y; bv[4 * q4 + 2] = bb.z; bv[4 * q4 + 3] = bb.w;
-          }
-          float col[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int i = c + j;
-            d = (i > u) ? d * e1v[j] : 1.f;
-            col[j] = (i > u && i < n) ? bv[j] * __uint_as_float(r[i]) * d : 0.f;
-          }
-#pragma unroll
-          for (int j = 0; j < 16; ++j) A[c + j][u] = col[j];
-        }
-      } else {
-        // Lane 64+i holds row i of Q K^T: P[i][j] = QK_ij exp(G_i - G_j),
-        // j <= i < n, decay as a running product towards smaller j.
-        const int i = u - 64;
-        float d = 1.f;
-        uint32_t w[32];
-#pragma unroll
-        for (int c = 48; c >= 0; c -= 16) {
-          float e1v[16];
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const float4 ev = *reinterpret_cast<const float4*>(&sm.e1[grp][c + 4 * q4]);
-            e1v[4 * q4] = ev.x; e1v[4 * q4 + 1] = ev.y; e1v[4 * q4 + 2] = ev.z; e1v[4 * q4 + 3] = ev.w;
-          }
-#pragma unroll
-          for (int jj = 15; jj >= 0; --jj) {
-            const int j = c + jj;
-            const float pj = (j <= i && i < n) ? __uint_as_float(r[j]) * d : 0.f;
-            d = (j <= i) ? d * e1v[jj] : 1.f;
-            if (j & 1) w[j >> 1] = __float_as_uint(pj);
-            else w[j >> 1] = pack_bf16x2(pj, __uint_as_float(w[j >> 1]));
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(rec + kRecP + sw128_chunk(i, c)) =
-              make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-      }
-    }
-    group_barrier(1 + grp, 128);
 
-    // T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution
-    // (one thread per block column), then block rows I = 1..3:
-    //   T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ.
-    const bool diag = active && ok && u < 64;
-    const int bl = u >> 4, dc = u & 15, o = bl * 16;
-    float x[16];
-    if (diag) {
+    if (threadIdx.x == 0) {
+      // D[128 x 64] = [K;Q] K^T: lanes 0-63 hold K K^T, lanes 64-127 Q K^T.
+      constexpr uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
+      const uint32_t t = smem_u32(sm.kq[buf]);
 #pragma unroll
-      for (int rr = 0; rr < 16; ++rr) {
-        float acc = (rr == dc) ? 1.f : 0.f;
-#pragma unroll
-        for (int m = 0; m < rr; ++m) acc -= A[o + rr][o + m] * x[m];
-        x[rr] = acc;
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * 16384u + (kk & 3) * 32u;
+        umma_bf16(tmem, umma_sdesc(t + off, 16, 1024), umma_sdesc(t + off, 16, 1024), idesc,
+                  kk > 0 ? 1u : 0u);
+      }
+      umma_commit(&sm.mma);
+      // The [K;Q] image to its record.
+      bulk_store(kq_records + static_cast<int64_t>(unit) * kKQBytes, sm.kq[buf], kKQBytes);
+      bulk_commit();
+      // Next unit into the other buffer, once the previous unit's store has
+      // read it (its MMA completed during the previous unit).
+      const int next = unit + gridDim.x;
+      if (next < units) {
+        bulk_wait_read<1>();
+        load_unit(next, buf ^ 1);
       }
     }
-    group_barrier(1 + grp, 128);  // every read of the diagonal A blocks is done
-    if (diag) {
-#pragma unroll
-      for (int rr = 0; rr < 16; ++rr) T[o + rr][o + dc] = x[rr];
-    }
-    group_barrier(1 + grp, 128);
-    merge_block_row<1>(A, T, X, u, grp, active && ok);
-    merge_block_row<2>(A, T, X, u, grp, active && ok);
-    merge_block_row<3>(A, T, X, u, grp, active && ok);
-    // Store T as K-rows j of the MN-major operand image (hi/lo pair):
-    // thread -> column j = u / 2, rows [32 (u % 2), +32).
-    if (active && ok) {
-      const int j = u >> 1;
-      const int i0 = (u & 1) * 32;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int p = 0; p < 4; ++p)
-          split_bf16x2(T[i0 + 8 * c + 2 * p][j], T[i0 + 8 * c + 2 * p + 1][j], hi[p], lo[p]);
-        const uint32_t off = sw128_chunk(j, (i0 >> 3) + c);
-        *reinterpret_cast<uint4*>(rec + kRecTHi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(rec + kRecTLo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+
+    bool ok = true;
+    bool waited = false;
+    // T overwrites A in place: block row I of A is last read while block row
+    // I of T is formed, and T's strictly upper part equals A's (zero).
+    float (*A)[68] = sm.amat[grp];
+    float (*T)[68] = sm.amat[grp];
+    float (*X)[52] = sm.xs[grp];
+
+    for (int hp = 0; hp < group; hp += 2) {
+      const int hl = hp + grp;
+      const bool active = hl < group;
+      const int h = kh * group + (active ? hl : 0);
+      uint8_t* rec = records + (static_cast<int64_t>(chunk) * value_heads + h) * kRecBytes;
+      float* fac = reinterpret_cast<float*>(rec + kRecF);
+
+      // Gating (aclnnFusedGdnGating: softplus beta 1, threshold 20) and the
+      // in-chunk cumsum as two warp scans.
+      if (active && u < 64) {
+        float ga = pre_a, gb = pre_b, alog = pre_alog, dtb = pre_dt;
+        if (hp > 0) {
+          alog = A_log[h];
+          dtb = dt_bias[h];
+          if (u < n) {
+            const int64_t gi = static_cast<int64_t>(t0 + u) * value_heads + h;
+            ga = bf16_bits_to_f32(a[gi]);
+            gb = bf16_bits_to_f32(b[gi]);
+          }
+        }
+        float g = 0.f, bt = 0.f;
+        if (u < n) {
+          g = -expf(alog) * softplus20(ga + dtb);
+          bt = round_bf16(1.0f / (1.0f + expf(-gb)));
+        }
+        sm.e1[grp][u] = __expf(g);
+  #pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, g, o);
+          if (lane >= o) g += y;
+        }
+        if (u == 31) sm.carry[grp] = g;
+        sm.beta[grp][u] = bt;
+        sm.g[grp][u] = g;
       }
+      group_barrier(1 + grp, 128);
+      if (active && u >= 32 && u < 64) sm.g[grp][u] += sm.carry[grp];
+      group_barrier(1 + grp, 128);
+      if (active && u < 64) {
+        const float gi = sm.g[grp][u];
+        const float glast = sm.g[grp][n - 1];
+        const float bt = sm.beta[grp][u];
+        const float egi = __expf(gi);
+        fac[kFBeta + u] = bt;
+        fac[kFBetaEG + u] = bt * egi;
+        fac[kFEG + u] = egi;
+        fac[kFED + u] = __expf(glast - gi);
+        if (u == 0) fac[kFELast] = __expf(glast);
+      }
+
+      if (!waited) {
+        ok = mbar_wait(&sm.mma, it & 1, err);
+        waited = true;
+      }
+      tmem_fence_after();
+      if (active && ok) {
+        const uint32_t base = tmem_addr(tmem, quarter * 32, 0);
+        uint32_t r[64];
+  #pragma unroll
+        for (int c = 0; c < 64; c += 16) {
+          uint32_t* rc = r + c;
+          tmem_ld16(base + c, *reinterpret_cast<uint32_t(*)[16]>(rc));
+        }
+        tmem_ld_wait();
+        if (u < 64) {
+          // Lane u holds row u of K K^T = column u (symmetric).  Column u of A:
+          // A[i][u] = beta_i KK_iu exp(G_i - G_u) for u < i < n, with the decay
+          // formed as a running product of the per-token exp(g).  The factors
+          // are read into registers first so the loop carries no shared-memory
+          // loads behind the stores to A.
+          float d = 1.f;
+  #pragma unroll
+          for (int c = 0; c < 64; c += 16) {
+            float e1v[16], bv[16];
+  #pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              const float4 ev = *reinterpret_cast<const float4*>(&sm.e1[grp][c + 4 * q4]);
+              const float4 bb = *reinterpret_cast<const float4*>(&sm.beta[grp][c + 4 * q4]);
+              e1v[4 * q4] = ev.x; e1v[4 * q4 + 1] = ev.y; e1v[4 * q4 + 2] = ev.z; e1v[4 * q4 + 3] = ev.w;
+              bv[4 * q4] = bb.x; bv[4 * q4 + 1] = bb.y; bv[4 * q4 + 2] = bb.z; bv[4 * q4 + 3] = bb.w;
+            }
+            float col[16];
+  #pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int i = c + j;
+              d = (i > u) ? d * e1v[j] : 1.f;
+              col[j] = (i > u && i < n) ? bv[j] * __uint_as_float(r[i]) * d : 0.f;
+            }
+  #pragma unroll
+            for (int j = 0; j < 16; ++j) A[c + j][u] = col[j];
+          }
+        } else {
+          // Lane 64+i holds row i of Q K^T: P[i][j] = QK_ij exp(G_i - G_j),
+          // j <= i < n, decay as a running product towards smaller j.
+          const int i = u - 64;
+          float d = 1.f;
+          uint32_t w[32];
+  #pragma unroll
+          for (int c = 48; c >= 0; c -= 16) {
+            float e1v[16];
+  #pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              const float4 ev = *reinterpret_cast<const float4*>(&sm.e1[grp][c + 4 * q4]);
+              e1v[4 * q4] = ev.x; e1v[4 * q4 + 1] = ev.y; e1v[4 * q4 + 2] = ev.z; e1v[4 * q4 + 3] = ev.w;
+            }
+  #pragma unroll
+            for (int jj = 15; jj >= 0; --jj) {
+              const int j = c + jj;
+              const float pj = (j <= i && i < n) ? __uint_as_float(r[j]) * d : 0.f;
+              d = (j <= i) ? d * e1v[jj] : 1.f;
+              if (j & 1) w[j >> 1] = __float_as_uint(pj);
+              else w[j >> 1] = pack_bf16x2(pj, __uint_as_float(w[j >> 1]));
+            }
+          }
+  #pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(rec + kRecP + sw128_chunk(i, c)) =
+                make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+        }
+      }
+      group_barrier(1 + grp, 128);
+
+      // T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution
+      // (one thread per block column), then block rows I = 1..3:
+      //   T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ.
+      const bool diag = active && ok && u < 64;
+      const int bl = u >> 4, dc = u & 15, o = bl * 16;
+      float x[16];
+      if (diag) {
+  #pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+          float acc = (rr == dc) ? 1.f : 0.f;
+  #pragma unroll
+          for (int m = 0; m < rr; ++m) acc -= A[o + rr][o + m] * x[m];
+          x[rr] = acc;
+        }
+      }
+      group_barrier(1 + grp, 128);  // every read of the diagonal A blocks is done
+      if (diag) {
+  #pragma unroll
+        for (int rr = 0; rr < 16; ++rr) T[o + rr][o + dc] = x[rr];
+      }
+      group_barrier(1 + grp, 128);
+      merge_block_row<1>(A, T, X, u, grp, active && ok);
+      merge_block_row<2>(A, T, X, u, grp, active && ok);
+      merge_block_row<3>(A, T, X, u, grp, active && ok);
+      // Store T as K-rows j of the MN-major operand image (hi/lo pair):
+      // thread -> column j = u / 2, rows [32 (u % 2), +32).
+      if (active && ok) {
+        const int j = u >> 1;
+        const int i0 = (u & 1) * 32;
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t hi[4], lo[4];
+  #pragma unroll
+          for (int p = 0; p < 4; ++p)
+            split_bf16x2(T[i0 + 8 * c + 2 * p][j], T[i0 + 8 * c + 2 * p + 1][j], hi[p], lo[p]);
+          const uint32_t off = sw128_chunk(j, (i0 >> 3) + c);
+          *reinterpret_cast<uint4*>(rec + kRecTHi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(rec + kRecTLo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+      }
+      group_barrier(1 + grp, 128);
     }
-    group_barrier(1 + grp, 128);
+    __syncthreads();   // shared scratch is reused by the next unit
   }
+  if (threadIdx.x == 0) bulk_wait_all();
   tmem_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -428,9 +476,9 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab, const uint16_t* __
 
 // =========================================================== state =====
 
-constexpr int kStateThreads = 288;  // warps 0-7 compute, warp 8 loads
+constexpr int kStateThreads = 256;  // eight warps; thread 0 also issues loads and MMAs
 constexpr int kDvHalf = 64;         // value columns per CTA
-constexpr int kDvGroup = 32;        // value columns per compute group
+constexpr int kDvGroup = 32;        // value columns per thread
 
 // One load stage: [K;Q] image, an 8 KB zero block, then the prep record
 // (P directly after the zeros so that [0;P] is one 128-row K-major tile),
@@ -443,34 +491,29 @@ constexpr uint32_t kStageBytes = kStV + 8192;       // 75776
 constexpr uint32_t kStageTx = kKQBytes + kRecBytes + 8192;
 static_assert(kStRec + kRecBytes <= kStV, "stage layout");
 
+// Operand images (128-byte-swizzled MN-major, 64 value columns per K row).
+// R and Vd keep their hi and lo halves 8 KB apart so that one N=128 operand
+// (LBO 8 KB) carries both: T_hi [R_hi | R_lo] and K^T [Vd_hi | Vd_lo] are
+// single products.
 struct StateSmemLayout {
   static constexpr uint32_t kStage0 = 0;
   static constexpr uint32_t kStage1 = kStageBytes;
-  static constexpr uint32_t kSop = 2 * kStageBytes;   // MN-major [128 dk x 64 dv]
-  static constexpr uint32_t kRhi = kSop + 16384;      // MN-major [64 tok x 64 dv]
-  static constexpr uint32_t kRlo = kRhi + 8192;
-  static constexpr uint32_t kVn = kRlo + 8192;
-  static constexpr uint32_t kVdhi = kVn + 8192;
-  static constexpr uint32_t kVdlo = kVdhi + 8192;
+  static constexpr uint32_t kSop = 2 * kStageBytes;   // S [128 dk x 64 dv] bf16
+  static constexpr uint32_t kRhi = kSop + 16384;      // R [64 tok x 64 dv] hi
+  static constexpr uint32_t kRlo = kRhi + 8192;       //                    lo
+  static constexpr uint32_t kVn = kRlo + 8192;        // v_new bf16
+  static constexpr uint32_t kVdhi = kVn + 8192;       // v_new exp(G_C - G) hi
+  static constexpr uint32_t kVdlo = kVdhi + 8192;     //                    lo
   static constexpr uint32_t kBars = kVdlo + 8192;
-  static constexpr uint32_t kTotal = kBars + 64 + 1024;
+  static constexpr uint32_t kTotal = kBars + 128 + 1024;
 };
 
-// TMEM columns: D1 [K;Q] S, D3 T R (M=64), D4 [0;P] v_new, D5 K^T Vd.
-constexpr uint32_t kTmD1 = 0, kTmD3 = 64, kTmD4 = 128, kTmD5 = 192;
+// TMEM columns: two [K;Q] S accumulators (alternate chunks, 64 each),
+// T [R_hi | R_lo] (M=64, 128), [0;P] v_new (64), K^T [Vd_hi | Vd_lo] (128).
+constexpr uint32_t kTmD1 = 0, kTmD3 = 128, kTmD4 = 256, kTmD5 = 320;
 
 __device__ __forceinline__ void compute_barrier() {
   asm volatile("bar.sync 1, 256;" ::: "memory");
-}
-
-// Wait used by the compute warps: thread 0 waits (bounded), the result is
-// broadcast through shared memory behind the compute barrier, so every
-// compute thread takes the same branch and none is left at a barrier.
-__device__ __forceinline__ bool compute_wait(uint64_t* bar, uint32_t parity, uint32_t* err,
-                                             volatile uint32_t* flag) {
-  if (threadIdx.x == 0) *flag = mbar_wait(bar, parity, err) ? 1u : 0u;
-  compute_barrier();
-  return *flag != 0u;
 }
 
 __global__ void __launch_bounds__(kStateThreads, 1)
@@ -485,10 +528,11 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBars);
-  uint64_t* empty = full + 2;
-  uint64_t* mma_bar = empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
-  volatile uint32_t* wait_flag = tmem_slot + 1;
+  uint64_t* smma = full + 2;       // per stage: the tensor core is done with it
+  uint64_t* mma_bar = smma + 2;
+  uint64_t* fin_bar = mma_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin_bar + 1);
+  volatile uint32_t* wait_flags = tmem_slot + 1;  // two alternating slots
 
   const int dvh = blockIdx.x;
   const int h = blockIdx.y;
@@ -502,67 +546,69 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
   const int nchunks = (seq_len + kChunk - 1) / kChunk;
   const int chunk0 = tab.chunk_start[seq];
 
+  // Stage loads: [K;Q] image and prep record (bulk copies), v (TMA).
+  auto load_stage = [&](int c) {
+    const int st = c & 1;
+    uint8_t* sb = smem + (st ? L::kStage1 : L::kStage0);
+    const int chunk = chunk0 + c;
+    mbar_arrive_expect_tx(&full[st], kStageTx);
+    bulk_load(sb + kStKQ, kq_records + (static_cast<int64_t>(chunk) * qk_heads + kh) * kKQBytes,
+              kKQBytes, &full[st]);
+    bulk_load(sb + kStRec, records + (static_cast<int64_t>(chunk) * value_heads + h) * kRecBytes,
+              kRecBytes, &full[st]);
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(sb + kStV)),
+        "l"(reinterpret_cast<uint64_t>(&tm_v)), "r"(smem_u32(&full[st])),
+        "r"(dvh * kDvHalf), "r"(h), "r"(seq_t0 + c * kChunk)
+        : "memory");
+  };
+  int issued = 0;    // chunks whose stage loads were issued (thread 0)
   if (tid == 0) {
     mbar_init(&full[0], 1);
     mbar_init(&full[1], 1);
-    mbar_init(&empty[0], 1);
-    mbar_init(&empty[1], 1);
+    mbar_init(&smma[0], 1);
+    mbar_init(&smma[1], 1);
     mbar_init(mma_bar, 1);
+    mbar_init(fin_bar, 1);
     fence_barrier_init();
     tma_prefetch_desc(&tm_v);
+    for (; issued < 2 && issued < nchunks; ++issued) load_stage(issued);
   }
-  if (warp == 0) tmem_alloc(tmem_slot, 256);
+  if (warp == 0) tmem_alloc(tmem_slot, 512);
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
-    // ------------------------------------------------------ loader warp --
-    if (lane == 0) {
-      int issued = 0;
-      for (int c = 0; c < nchunks; ++c) {
-        const int st = c & 1;
-        if (!mbar_wait(&empty[st], ((c >> 1) & 1) ^ 1u, err)) break;
-        uint8_t* sb = smem + (st ? L::kStage1 : L::kStage0);
-        const int chunk = chunk0 + c;
-        mbar_arrive_expect_tx(&full[st], kStageTx);
-        bulk_load(sb + kStKQ, kq_records + (static_cast<int64_t>(chunk) * qk_heads + kh) * kKQBytes,
-                  kKQBytes, &full[st]);
-        bulk_load(sb + kStRec, records + (static_cast<int64_t>(chunk) * value_heads + h) * kRecBytes,
-                  kRecBytes, &full[st]);
-        asm volatile(
-            "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-            " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(sb + kStV)),
-            "l"(reinterpret_cast<uint64_t>(&tm_v)), "r"(smem_u32(&full[st])),
-            "r"(dvh * kDvHalf), "r"(h), "r"(seq_t0 + c * kChunk)
-            : "memory");
-        issued = c + 1;
-      }
-      // If the launch failed, let copies still in flight land before exit.
-      if (err != nullptr && *reinterpret_cast<volatile uint32_t*>(err) != 0) {
-        for (int c = (issued > 2 ? issued - 2 : 0); c < issued; ++c) {
-          const unsigned long long t_start = global_ns();
-          while (!mbar_try_wait(&full[c & 1], (c >> 1) & 1) &&
-                 global_ns() - t_start < kWaitLimitNs) {
-          }
-        }
-      }
-    }
-  } else {
+  {
     // ---------------------------------------------------- compute warps --
     const float scale = 0.08838834764831845f;
     const int cg = warp >> 2;             // column group: value columns [32 cg, 32 cg + 32)
     const int quarter = warp & 3;         // TMEM lane quarter
     const int lrow = quarter * 32 + lane; // TMEM lane of this thread
     const int c0 = cg * kDvGroup;
+    const bool leader = tid == 0;         // issues every MMA
     uint8_t* sop = smem + L::kSop;
     uint8_t* rhi = smem + L::kRhi;
     uint8_t* rlo = smem + L::kRlo;
     uint8_t* vn = smem + L::kVn;
     uint8_t* vdhi = smem + L::kVdhi;
     uint8_t* vdlo = smem + L::kVdlo;
-    const int ct = tid;                   // 0..255 among compute threads
+
+    // Bounded wait shared by the compute threads: the leader waits (only if
+    // `pre` holds) and the outcome reaches every compute thread through
+    // shared memory behind the compute barrier, so all take the same branch.
+    // Two flag slots alternate so a slot is rewritten only after a later
+    // barrier.
+    uint32_t nwaits = 0;
+    auto compute_wait = [&](uint64_t* bar, uint32_t parity, bool pre) -> bool {
+      volatile uint32_t* f = wait_flags + (nwaits & 1u);
+      ++nwaits;
+      if (leader) *f = (pre && mbar_wait(bar, parity, err)) ? 1u : 0u;
+      compute_barrier();
+      return *f != 0u;
+    };
 
     // State: thread owns key row lrow, value columns dvh*64 + c0 + [0, 32).
     float s[kDvGroup];
@@ -581,9 +627,39 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
         *reinterpret_cast<uint4*>(sop + sw128_chunk(lrow, (c0 >> 3) + cc)) = w;
       }
     };
+
+    // Output rows of a finished chunk (lanes 64..127, row i = lrow - 64):
+    // O = scale (exp(G_i) (Q S)_i + (P v_new)_i).
+    int prev_t0 = 0, prev_n = 0;
+    float prev_eg = 0.f;
+    auto write_output = [&](uint32_t d1) {
+      const int i = lrow - 64;
+      uint32_t rq[2][16], rp[2][16];
+      tmem_ld16(tmem_addr(d1, quarter * 32, c0), rq[0]);
+      tmem_ld16(tmem_addr(d1, quarter * 32, c0 + 16), rq[1]);
+      tmem_ld16(tmem_addr(tmem + kTmD4, quarter * 32, c0), rp[0]);
+      tmem_ld16(tmem_addr(tmem + kTmD4, quarter * 32, c0 + 16), rp[1]);
+      tmem_ld_wait();
+      if (i < prev_n) {
+        uint16_t* orow = o_out + (static_cast<int64_t>(prev_t0 + i) * value_heads + h) * kHeadDim +
+                         dvh * kDvHalf + c0;
+        uint32_t w[16];
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+          const int e = 2 * p;
+          const float o0 = scale * (prev_eg * __uint_as_float(rq[e >> 4][e & 15]) + __uint_as_float(rp[e >> 4][e & 15]));
+          const float o1 = scale * (prev_eg * __uint_as_float(rq[e >> 4][(e & 15) + 1]) + __uint_as_float(rp[e >> 4][(e & 15) + 1]));
+          w[p] = pack_bf16x2(o0, o1);
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+          reinterpret_cast<uint4*>(orow)[q4] = make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+      }
+    };
+
     write_sop();
     // Zero blocks in front of P in both stages (never written by the loader).
-    for (int e = ct; e < 2 * 8192 / 16; e += 256) {
+    for (int e = tid; e < 2 * 8192 / 16; e += 256) {
       const int st = e / 512;
       reinterpret_cast<uint4*>(smem + (st ? L::kStage1 : L::kStage0) + kStZero)[e % 512] =
           make_uint4(0u, 0u, 0u, 0u);
@@ -593,112 +669,136 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
 
     uint32_t mma_phase = 0;
     bool ok = true;
-    for (int c = 0; c < nchunks && ok; ++c) {
+    bool lead_ok = true;   // thread 0: every wait of its own succeeded
+    int consumed = 0;      // chunks whose stage was seen landed
+    for (int c = 0; c < nchunks; ++c) {
       const int st = c & 1;
       uint8_t* sb = smem + (st ? L::kStage1 : L::kStage0);
       const float* fac = reinterpret_cast<const float*>(sb + kStRec + kRecF);
       const int t0 = seq_t0 + c * kChunk;
       const int n = min(kChunk, seq_t0 + seq_len - t0);
-      if (!compute_wait(&full[st], (c >> 1) & 1, err, wait_flag)) { ok = false; break; }
+      const uint32_t d1 = tmem + kTmD1 + (c & 1) * 64;
+      const uint32_t d1_prev = tmem + kTmD1 + ((c & 1) ^ 1) * 64;
 
-      // D1 = [K;Q] S  (M=128, N=64, K=128; S as MN-major B).
-      if (ct == 0) {
-        tmem_fence_after();
-        constexpr uint32_t id = umma_idesc_bf16(128, 64, false, true);
-        const uint32_t akq = smem_u32(sb + kStKQ);
-        const uint32_t bs = smem_u32(sop);
+      // D1 = [K;Q] S  (M=128, N=64, K=128; S as MN-major B), once the stage
+      // has landed.
+      bool landed = lead_ok;
+      if (leader && landed) {
+        landed = mbar_wait(&full[st], (c >> 1) & 1, err);
+        if (landed) {
+          tmem_fence_after();
+          constexpr uint32_t id = umma_idesc_bf16(128, 64, false, true);
+          const uint32_t akq = smem_u32(sb + kStKQ);
+          const uint32_t bs = smem_u32(sop);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          umma_bf16(tmem + kTmD1, umma_sdesc(akq + (kk >> 2) * 16384u + (kk & 3) * 32u, 16, 1024),
-                    umma_sdesc(bs + kk * 2048u, 16384, 1024), id, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 8; ++kk) {
+            umma_bf16(d1, umma_sdesc(akq + (kk >> 2) * 16384u + (kk & 3) * 32u, 16, 1024),
+                      umma_sdesc(bs + kk * 2048u, 16384, 1024), id, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(mma_bar);
+          // The stage of chunk c - 1 takes chunk c + 1 once the MMAs reading
+          // it have completed (every thread finished with it at the end of
+          // chunk c - 1); done here, while the MMAs above run.
+          if (c >= 1 && c + 1 < nchunks) {
+            lead_ok = mbar_wait(&smma[st ^ 1], ((c - 1) >> 1) & 1, err);
+            if (lead_ok) {
+              load_stage(c + 1);
+              issued = c + 2;
+            }
+            landed = lead_ok;
+          }
         }
-        umma_commit(mma_bar);
       }
-      if (!compute_wait(mma_bar, mma_phase, err, wait_flag)) { ok = false; break; }
+      // Completion of this commit also covers the previous chunk's [0;P] v_new.
+      if (!compute_wait(mma_bar, mma_phase, landed)) { ok = false; break; }
+      consumed = c + 1;
       mma_phase ^= 1u;
       tmem_fence_after();
 
-      // R = beta V - beta exp(G) (K S) for token rows (lanes 0-63).
       if (quarter < 2) {
+        // R = beta V - beta exp(G) (K S) for token rows (lanes 0-63).
         const int i = lrow;
+        uint32_t r[2][16];
+        tmem_ld16(tmem_addr(d1, quarter * 32, c0), r[0]);
+        tmem_ld16(tmem_addr(d1, quarter * 32, c0 + 16), r[1]);
         const float bi = fac[kFBeta + i], begi = fac[kFBetaEG + i];
-        const uint8_t* vt = sb + kStV;
+        uint4 vv[4];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t r[16];
-          tmem_ld16(tmem_addr(tmem, quarter * 32, kTmD1 + c0 + 16 * half), r);
-          tmem_ld_wait();
+        for (int q4 = 0; q4 < 4; ++q4)
+          vv[q4] = *reinterpret_cast<const uint4*>(sb + kStV + sw128_chunk(i, (c0 >> 3) + q4));
+        tmem_ld_wait();
 #pragma unroll
-          for (int q8 = 0; q8 < 2; ++q8) {
-            const int jc = (c0 >> 3) + 2 * half + q8;   // 8-column chunk
-            const uint4 vv = *reinterpret_cast<const uint4*>(vt + sw128_chunk(i, jc));
-            const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
-            uint32_t hi[4], lo[4];
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const uint32_t vw[4] = {vv[q4].x, vv[q4].y, vv[q4].z, vv[q4].w};
+          uint32_t hi[4], lo[4];
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
-              const float r0 = bi * bf16lo_f32(vw[p]) - begi * __uint_as_float(r[8 * q8 + 2 * p]);
-              const float r1 = bi * bf16hi_f32(vw[p]) - begi * __uint_as_float(r[8 * q8 + 2 * p + 1]);
-              split_bf16x2(r0, r1, hi[p], lo[p]);
-            }
-            *reinterpret_cast<uint4*>(rhi + sw128_chunk(i, jc)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4*>(rlo + sw128_chunk(i, jc)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          for (int p = 0; p < 4; ++p) {
+            const int e = 8 * q4 + 2 * p;
+            const float r0 = bi * bf16lo_f32(vw[p]) - begi * __uint_as_float(r[e >> 4][e & 15]);
+            const float r1 = bi * bf16hi_f32(vw[p]) - begi * __uint_as_float(r[e >> 4][(e & 15) + 1]);
+            split_bf16x2(r0, r1, hi[p], lo[p]);
           }
+          const uint32_t off = sw128_chunk(i, (c0 >> 3) + q4);
+          *reinterpret_cast<uint4*>(rhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(rlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
+      } else if (c > 0) {
+        write_output(d1_prev);   // previous chunk, off the state chain
       }
       fence_proxy_async_smem();
       tmem_fence_before();
       compute_barrier();
 
-      // D3 = T_hi R_hi + T_lo R_hi + T_hi R_lo = v_new  (M=64, A MN-major).
-      if (ct == 0) {
+      // D3[:, 0:64] = T_hi R_hi + T_lo R_hi, D3[:, 64:128] = T_hi R_lo
+      // (M=64, A MN-major); v_new = D3[:, j] + D3[:, 64 + j].
+      if (leader) {
         tmem_fence_after();
-        constexpr uint32_t id = umma_idesc_bf16(64, 64, true, true);
+        constexpr uint32_t id_w = umma_idesc_bf16(64, 128, true, true);
+        constexpr uint32_t id_n = umma_idesc_bf16(64, 64, true, true);
         const uint32_t thi = smem_u32(sb + kStRec + kRecTHi);
         const uint32_t tlo = smem_u32(sb + kStRec + kRecTLo);
-        const uint32_t bh = smem_u32(rhi), bl = smem_u32(rlo);
+        const uint32_t br = smem_u32(rhi);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           umma_bf16(tmem + kTmD3, umma_sdesc(thi + kk * 2048, 8192, 1024),
-                    umma_sdesc(bh + kk * 2048, 8192, 1024), id, kk > 0 ? 1u : 0u);
+                    umma_sdesc(br + kk * 2048, 8192, 1024), id_w, kk > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < 4; ++kk)
           umma_bf16(tmem + kTmD3, umma_sdesc(tlo + kk * 2048, 8192, 1024),
-                    umma_sdesc(bh + kk * 2048, 8192, 1024), id, 1u);
-          umma_bf16(tmem + kTmD3, umma_sdesc(thi + kk * 2048, 8192, 1024),
-                    umma_sdesc(bl + kk * 2048, 8192, 1024), id, 1u);
-        }
+                    umma_sdesc(br + kk * 2048, 8192, 1024), id_n, 1u);
         umma_commit(mma_bar);
       }
-      if (!compute_wait(mma_bar, mma_phase, err, wait_flag)) { ok = false; break; }
+      if (!compute_wait(mma_bar, mma_phase, true)) { ok = false; break; }
       mma_phase ^= 1u;
       tmem_fence_after();
 
-      // v_new rows (M=64 layout: row 16*quarter + lane, lane < 16):
-      // bf16 v_new, and v_new exp(G_C - G) as a hi/lo pair.
+      // v_new rows (M=64 layout: row 16*quarter + lane, lane < 16): bf16
+      // v_new, and v_new exp(G_C - G) as a hi/lo pair.
       {
         const int i = quarter * 16 + lane;
+        uint32_t ra[2][16], rb[2][16];
+        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, c0), ra[0]);
+        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, c0 + 16), ra[1]);
+        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, 64 + c0), rb[0]);
+        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, 64 + c0 + 16), rb[1]);
         const float edi = (lane < 16) ? fac[kFED + i] : 0.f;
+        tmem_ld_wait();
+        if (lane < 16) {
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t r[16];
-          tmem_ld16(tmem_addr(tmem, quarter * 32, kTmD3 + c0 + 16 * half), r);
-          tmem_ld_wait();
-          if (lane < 16) {
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint32_t vb[4], dh[4], dl[4];
 #pragma unroll
-            for (int q8 = 0; q8 < 2; ++q8) {
-              const int jc = (c0 >> 3) + 2 * half + q8;
-              uint32_t vb[4], dh[4], dl[4];
-#pragma unroll
-              for (int p = 0; p < 4; ++p) {
-                const float v0 = __uint_as_float(r[8 * q8 + 2 * p]);
-                const float v1 = __uint_as_float(r[8 * q8 + 2 * p + 1]);
-                vb[p] = pack_bf16x2(v0, v1);
-                split_bf16x2(v0 * edi, v1 * edi, dh[p], dl[p]);
-              }
-              *reinterpret_cast<uint4*>(vn + sw128_chunk(i, jc)) = make_uint4(vb[0], vb[1], vb[2], vb[3]);
-              *reinterpret_cast<uint4*>(vdhi + sw128_chunk(i, jc)) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
-              *reinterpret_cast<uint4*>(vdlo + sw128_chunk(i, jc)) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
+            for (int p = 0; p < 4; ++p) {
+              const int e = 8 * q4 + 2 * p;
+              const float v0 = __uint_as_float(ra[e >> 4][e & 15]) + __uint_as_float(rb[e >> 4][e & 15]);
+              const float v1 = __uint_as_float(ra[e >> 4][(e & 15) + 1]) + __uint_as_float(rb[e >> 4][(e & 15) + 1]);
+              vb[p] = pack_bf16x2(v0, v1);
+              split_bf16x2(v0 * edi, v1 * edi, dh[p], dl[p]);
             }
+            const uint32_t off = sw128_chunk(i, (c0 >> 3) + q4);
+            *reinterpret_cast<uint4*>(vn + off) = make_uint4(vb[0], vb[1], vb[2], vb[3]);
+            *reinterpret_cast<uint4*>(vdhi + off) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
+            *reinterpret_cast<uint4*>(vdlo + off) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
           }
         }
       }
@@ -706,77 +806,69 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
       tmem_fence_before();
       compute_barrier();
 
-      // D4 = [0;P] v_new (M=128), D5 = K^T (Vd_hi + Vd_lo) (M=128, A MN-major).
-      if (ct == 0) {
+      // D5 = K^T [Vd_hi | Vd_lo] (M=128, N=128, A MN-major): the state chain.
+      // Then D4 = [0;P] v_new for the output, completed behind the next commit.
+      if (leader) {
         tmem_fence_after();
+        constexpr uint32_t id_s = umma_idesc_bf16(128, 128, true, true);
         constexpr uint32_t id_o = umma_idesc_bf16(128, 64, false, true);
-        constexpr uint32_t id_s = umma_idesc_bf16(128, 64, true, true);
-        const uint32_t ap = smem_u32(sb + kStZero);
         const uint32_t akt = smem_u32(sb + kStKQ);
-        const uint32_t bv = smem_u32(vn), bdh = smem_u32(vdhi), bdl = smem_u32(vdlo);
+        const uint32_t ap = smem_u32(sb + kStZero);
+        const uint32_t bv = smem_u32(vn), bd = smem_u32(vdhi);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          // A = K^T: MN-major view of the [K;Q] rows 0..63, dk slabs 16 KB apart.
+          umma_bf16(tmem + kTmD5, umma_sdesc(akt + kk * 2048, 16384, 1024),
+                    umma_sdesc(bd + kk * 2048, 8192, 1024), id_s, kk > 0 ? 1u : 0u);
+        umma_commit(mma_bar);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           umma_bf16(tmem + kTmD4, umma_sdesc(ap + kk * 32, 16, 1024),
                     umma_sdesc(bv + kk * 2048, 8192, 1024), id_o, kk > 0 ? 1u : 0u);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          // A = K^T: MN-major view of the [K;Q] rows 0..63, dk slabs 16 KB apart.
-          umma_bf16(tmem + kTmD5, umma_sdesc(akt + kk * 2048, 16384, 1024),
-                    umma_sdesc(bdh + kk * 2048, 8192, 1024), id_s, kk > 0 ? 1u : 0u);
-          umma_bf16(tmem + kTmD5, umma_sdesc(akt + kk * 2048, 16384, 1024),
-                    umma_sdesc(bdl + kk * 2048, 8192, 1024), id_s, 1u);
-        }
-        umma_commit(mma_bar);
+        umma_commit(&smma[st]);    // every MMA reading this stage has completed
       }
-      if (!compute_wait(mma_bar, mma_phase, err, wait_flag)) { ok = false; break; }
+      if (!compute_wait(mma_bar, mma_phase, true)) { ok = false; break; }
       mma_phase ^= 1u;
       tmem_fence_after();
 
-      // Output rows (lanes 64..127) and the state update (every lane).
-      if (quarter >= 2) {
-        const int i = lrow - 64;
-        const float egi = fac[kFEG + i];
-        uint16_t* orow = o_out + (static_cast<int64_t>(t0 + i) * value_heads + h) * kHeadDim +
-                         dvh * kDvHalf + c0;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t rq[16], rp[16];
-          tmem_ld16(tmem_addr(tmem, quarter * 32, kTmD1 + c0 + 16 * half), rq);
-          tmem_ld16(tmem_addr(tmem, quarter * 32, kTmD4 + c0 + 16 * half), rp);
-          tmem_ld_wait();
-          if (i < n) {
-            uint32_t w[8];
-#pragma unroll
-            for (int p = 0; p < 8; ++p) {
-              const float o0 = scale * (egi * __uint_as_float(rq[2 * p]) + __uint_as_float(rp[2 * p]));
-              const float o1 = scale * (egi * __uint_as_float(rq[2 * p + 1]) + __uint_as_float(rp[2 * p + 1]));
-              w[p] = pack_bf16x2(o0, o1);
-            }
-            reinterpret_cast<uint4*>(orow + 16 * half)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            reinterpret_cast<uint4*>(orow + 16 * half)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-          }
-        }
-      }
+      // State update (every lane): S = exp(G_C) S + K^T Vd_hi + K^T Vd_lo.
       {
+        uint32_t ra[2][16], rb[2][16];
+        tmem_ld16(tmem_addr(tmem + kTmD5, quarter * 32, c0), ra[0]);
+        tmem_ld16(tmem_addr(tmem + kTmD5, quarter * 32, c0 + 16), ra[1]);
+        tmem_ld16(tmem_addr(tmem + kTmD5, quarter * 32, 64 + c0), rb[0]);
+        tmem_ld16(tmem_addr(tmem + kTmD5, quarter * 32, 64 + c0 + 16), rb[1]);
         const float dl = fac[kFELast];
+        if (quarter >= 2) prev_eg = fac[kFEG + lrow - 64];
+        tmem_ld_wait();
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t r[16];
-          tmem_ld16(tmem_addr(tmem, quarter * 32, kTmD5 + c0 + 16 * half), r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) s[16 * half + j] = dl * s[16 * half + j] + __uint_as_float(r[j]);
-        }
+        for (int j = 0; j < kDvGroup; ++j)
+          s[j] = dl * s[j] + (__uint_as_float(ra[j >> 4][j & 15]) + __uint_as_float(rb[j >> 4][j & 15]));
         write_sop();
       }
+      prev_t0 = t0;
+      prev_n = n;
       fence_proxy_async_smem();
       tmem_fence_before();
       compute_barrier();
-      if (ct == 0) mbar_arrive(&empty[st]);   // stage fully consumed
     }
-    if (ok) {
+    // Drain: every MMA issued (the last [0;P] v_new included) completes
+    // before the last output, the state write and the TMEM release.
+    if (leader) umma_commit(fin_bar);
+    const bool drained = compute_wait(fin_bar, 0, true);
+    if (ok && drained) {
+      tmem_fence_after();
+      if (quarter >= 2 && nchunks > 0) write_output(tmem + kTmD1 + ((nchunks - 1) & 1) * 64);
 #pragma unroll
       for (int j = 0; j < kDvGroup; ++j) sg[(dvh * kDvHalf + c0 + j) * kHeadDim + lrow] = s[j];
+    }
+    // After a failure, let stage copies still in flight land before exit.
+    if (leader && !ok) {
+      for (int c = consumed; c < issued; ++c) {
+        const unsigned long long t_start = global_ns();
+        while (!mbar_try_wait(&full[c & 1], (c >> 1) & 1) && global_ns() - t_start < kWaitLimitNs) {
+        }
+      }
     }
   }
   tmem_fence_before();
@@ -784,7 +876,7 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
   if (warp == 0) {
     __syncwarp();
     tmem_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -858,18 +950,31 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
   const int64_t tokens = tab.cu[tab.num_seqs];
   uint8_t* kq_records = scratch;
   uint8_t* records = scratch + static_cast<uint64_t>(tab.total_chunks) * qk_heads * kKQBytes;
+  CUtensorMap tq, tk, tv;
+  if (!make_tmap_thd(&tq, q, tokens, qk_heads) || !make_tmap_thd(&tk, k, tokens, qk_heads) ||
+      !make_tmap_thd(&tv, v, tokens, value_heads))
+    return cudaErrorInvalidValue;
   const uint32_t prep_smem = sizeof(PrepSmem) + 1024;
   cudaError_t e = cudaFuncSetAttribute(gdn_chunk_prep_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem);
   if (e != cudaSuccess) return e;
-  dim3 pgrid(tab.total_chunks, qk_heads);
+  // All of L1 as shared memory, so that two CTAs fit on an SM.
+  e = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           100);
+  if (e != cudaSuccess) return e;
+  // Persistent grid: two CTAs per SM (128 registers x 256 threads and about
+  // 100 KB of shared memory each), at most one per unit.  CTAs never wait on
+  // one another, so fewer resident slots only means a second wave.
+  int device = 0, sms = 0;
+  if ((e = cudaGetDevice(&device)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return e;
+  const int64_t units = static_cast<int64_t>(tab.total_chunks) * qk_heads;
+  const int pgrid = static_cast<int>(std::min<int64_t>(units, 2 * static_cast<int64_t>(sms)));
   gdn_chunk_prep_kernel<<<pgrid, kPrepThreads, prep_smem, stream>>>(
-      tab, q, k, a, b, A_log, dt_bias, kq_records, records, qk_heads, value_heads, err);
+      tab, tq, tk, a, b, A_log, dt_bias, kq_records, records, qk_heads, value_heads, err);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  CUtensorMap tv;
-  if (!make_tmap_thd(&tv, v, tokens, value_heads)) return cudaErrorInvalidValue;
   const uint32_t st_smem = StateSmemLayout::kTotal;
   e = cudaFuncSetAttribute(gdn_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            st_smem);

@@ -74,6 +74,24 @@ __device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, u
   lo = pack_bf16x2(x0 - bf16lo_f32(hi), x1 - bf16hi_f32(hi));
 }
 
+// Packed f32x2 arithmetic (one instruction for two IEEE fp32 lanes).
+__device__ __forceinline__ unsigned long long f2_pack(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+// a * b + c per lane, rounded once (fma.rn).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)), "l"(f2_pack(c)));
+  return f2_unpack(d);
+}
+
 // ---------------------------------------------------------- mbarrier -----
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -100,16 +118,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait on a phase parity.  Returns false (and records the error) when
 // the limit runs out or another thread of the launch already failed.
+// The clock and the launch's error word (a global load of several hundred
+// cycles) are read once every 64 polls only, so a phase that completes is
+// seen within one poll instead of behind that load.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_ns();
-  while (true) {
+  for (uint32_t poll = 1;; ++poll) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - start > kWaitLimitNs) {
-      record_error(err, kErrWaitTimeout);
-      return false;
+    if ((poll & 63u) == 0u) {
+      if (global_ns() - start > kWaitLimitNs) {
+        record_error(err, kErrWaitTimeout);
+        return false;
+      }
+      if (err != nullptr && *reinterpret_cast<volatile uint32_t*>(err) != 0) return false;
     }
-    if (err != nullptr && *reinterpret_cast<volatile uint32_t*>(err) != 0) return false;
   }
 }
 
@@ -138,6 +161,38 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// 3-D tiled bulk tensor load into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map,
+                                            uint64_t* bar, int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// 1-D bulk copy shared -> global, tracked by the issuing thread's bulk
+// groups.  Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(gmem_dst)),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N of this thread's committed bulk groups still read
+// their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until every committed bulk group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // 1-D bulk copy global -> this CTA's shared memory (no multicast).  Both
 // addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
@@ -154,15 +209,24 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
 // UMMA shared-memory matrix descriptor (sm_100 layout: start >> 4 in [0,14),
 // LBO >> 4 in [16,30), SBO >> 4 in [32,46), version 1 in [46,48),
 // layout type in [61,64); 2 = 128-byte swizzle).
-__device__ __forceinline__ uint64_t umma_sdesc(uint32_t smem_addr, uint32_t lbo_bytes,
-                                               uint32_t sbo_bytes) {
+__device__ __forceinline__ uint64_t umma_sdesc_layout(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                      uint32_t sbo_bytes, uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
+}
+__device__ __forceinline__ uint64_t umma_sdesc(uint32_t smem_addr, uint32_t lbo_bytes,
+                                               uint32_t sbo_bytes) {
+  return umma_sdesc_layout(smem_addr, lbo_bytes, sbo_bytes, 2u);
+}
+// 64-byte-swizzled operand (layout type 4), see sw64_chunk.
+__device__ __forceinline__ uint64_t umma_sdesc_sw64(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  return umma_sdesc_layout(smem_addr, lbo_bytes, sbo_bytes, 4u);
 }
 
 // Instruction descriptor, kind::f16 with bf16 A/B and f32 accumulator.
@@ -261,6 +325,14 @@ __device__ __forceinline__ uint32_t mnmajor_offset(uint32_t k, uint32_t mn, uint
 // in one 128-byte-swizzled slab (same formula for both majors).
 __device__ __forceinline__ uint32_t sw128_chunk(uint32_t row, uint32_t j) {
   return (row >> 3) * 1024u + (row & 7u) * 128u + (((j ^ row) & 7u) << 4);
+}
+// 64-byte-swizzled MN-major operand of 32-element (64-byte) K rows: a
+// 512-byte atom holds 8 rows and the 16-byte chunk j (0..3) of row r sits at
+// chunk position j ^ ((r / 2) % 4), i.e. address bits [4,6) XOR bits [7,9).
+// Atoms start on a 512-byte boundary; descriptor SBO = 512 (8 K rows), the
+// K step of 16 rows adds 1024 bytes.
+__device__ __forceinline__ uint32_t sw64_chunk(uint32_t row, uint32_t j) {
+  return row * 64u + (((j ^ (row >> 1)) & 3u) << 4);
 }
 
 }  // namespace gdn
