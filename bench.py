@@ -39,6 +39,10 @@ SEQ_LEN = 4096
 SEQS_PER_GPU = 2
 QK_HEADS, V_HEADS, HIDDEN = 16, 32, 2048
 CHUNK_MFLOP = 11.62    # prefill core work per (chunk of 64, v-head)
+# DRAM bytes (read + write) per call of the chunk core on the single-GPU
+# workload, from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum
+# of the prep and state kernels on this workload).
+CHUNK_CORE_DRAM_BYTES = {"prep": 68445696 + 121025792, "state": 244360448 + 44962816}
 
 
 def load_peaks():
@@ -274,9 +278,16 @@ def main():
         "output_tail": {"ms": tail_ms, "tflops": tail_tf, "frac": tail_tf / tf_peak},
     }
     dom = "chunk_core" if core_ms >= tail_ms else "output_tail"
+    # Measured DRAM traffic is quoted for the single-GPU workload only (the
+    # per-rank shard of N GPUs has the same per-rank size, so it applies there
+    # too: weak scaling keeps every rank's kernels identical).
+    traffic = (sum(CHUNK_CORE_DRAM_BYTES.values()) if dom == "chunk_core" else None)
     roofline = {"bound": "tensor", "kernel": dom, "achieved": comps[dom]["tflops"],
                 "peak": tf_peak, "unit": "TFLOP/s", "frac": comps[dom]["frac"],
-                "peak_kind": f"{peak_kind} burst bf16", "traffic": None}
+                "peak_kind": f"{peak_kind} burst bf16", "traffic": traffic,
+                "traffic_unit": "bytes per call (ncu, prep + state kernels)",
+                "traffic_gbs": (traffic / (comps[dom]["ms"] * 1e-3) / 1e9) if traffic else None,
+                "hbm_peak_gbs": hbm_peak}
 
     # End to end through the provider ABI (the reference-facing plugin
     # interface): pinned host inputs -> device, submit, wait, output -> host.
