@@ -476,49 +476,89 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
 
 // =========================================================== state =====
 
-constexpr int kStateThreads = 256;  // eight warps; thread 0 also issues loads and MMAs
+// Eight compute warps, an MMA issuer warp and a loader warp.  Lane 0 of
+// warp 8 issues every MMA and waits on the tensor core; compute warps and
+// issuer hand over through named barriers (compute -> issuer: operands
+// ready; issuer -> compute: products ready, with an ok flag).  Lane 0 of
+// warp 9 issues the stage loads, the L2 prefetch and the output stores,
+// driven by mbarriers from the issuer.
+constexpr int kStateThreads = 320;
+constexpr int kSyncThreads = 288;       // compute warps + MMA issuer warp
+constexpr int kComputeThreads = 256;
 constexpr int kDvHalf = 64;         // value columns per CTA
-constexpr int kDvGroup = 32;        // value columns per thread
+constexpr int kDvGroup = 32;        // value columns per thread in the state update
 
-// One load stage: [K;Q] image, an 8 KB zero block, then the prep record
-// (P directly after the zeros so that [0;P] is one 128-row K-major tile),
-// then v ([64 tokens x 64] bf16, one 128-byte-swizzled TMA box).
+// One load stage: [K;Q] image, the prep record, then v ([64 tokens x 64]
+// bf16, one 128-byte-swizzled TMA box).
 constexpr uint32_t kStKQ = 0;
-constexpr uint32_t kStZero = kKQBytes;              // 32768
-constexpr uint32_t kStRec = kStZero + 8192;         // 40960
-constexpr uint32_t kStV = 67584;                    // 66 KB, after the record
-constexpr uint32_t kStageBytes = kStV + 8192;       // 75776
+constexpr uint32_t kStRec = kKQBytes;               // 32768
+constexpr uint32_t kStV = 59392;                    // 58 KB, after the record
+constexpr uint32_t kStageBytes = kStV + 8192;       // 67584
 constexpr uint32_t kStageTx = kKQBytes + kRecBytes + 8192;
 static_assert(kStRec + kRecBytes <= kStV, "stage layout");
 
-// Operand images (128-byte-swizzled MN-major, 64 value columns per K row).
-// R and Vd keep their hi and lo halves 8 KB apart so that one N=128 operand
-// (LBO 8 KB) carries both: T_hi [R_hi | R_lo] and K^T [Vd_hi | Vd_lo] are
-// single products.
+// Operand images, all 128-byte swizzled:
+//   S    MN-major [128 dk x 64 dv]     A of [S^T; S^T] [K;Q]^T (dv = M)
+//   R    K-major  [128 x 64 tokens]    rows 0-63 R_hi^T, 64-127 R_lo^T (dv rows)
+//   Vn   MN-major [64 tokens x 64 dv]  A of [Vn^T; Vn^T] P^T (dv = M)
+//   Vd   MN-major [64 tokens x 64 dv]  hi, then lo 8 KB later (one N=128 B)
+//   O    [64 tokens x 64 dv] bf16, two buffers: the output tile of a chunk,
+//        written to global memory by a TMA store
 struct StateSmemLayout {
   static constexpr uint32_t kStage0 = 0;
   static constexpr uint32_t kStage1 = kStageBytes;
-  static constexpr uint32_t kSop = 2 * kStageBytes;   // S [128 dk x 64 dv] bf16
-  static constexpr uint32_t kRhi = kSop + 16384;      // R [64 tok x 64 dv] hi
-  static constexpr uint32_t kRlo = kRhi + 8192;       //                    lo
-  static constexpr uint32_t kVn = kRlo + 8192;        // v_new bf16
-  static constexpr uint32_t kVdhi = kVn + 8192;       // v_new exp(G_C - G) hi
-  static constexpr uint32_t kVdlo = kVdhi + 8192;     //                    lo
-  static constexpr uint32_t kBars = kVdlo + 8192;
+  static constexpr uint32_t kSop = 2 * kStageBytes;   // 135168
+  static constexpr uint32_t kR = kSop + 16384;
+  static constexpr uint32_t kVn = kR + 16384;
+  static constexpr uint32_t kVdhi = kVn + 8192;
+  static constexpr uint32_t kVdlo = kVdhi + 8192;
+  static constexpr uint32_t kOut = kVdlo + 8192;      // two 8 KB tiles
+  static constexpr uint32_t kEg = kOut + 16384;       // exp(G) of the chunk awaiting output
+  static constexpr uint32_t kBars = kEg + 256;
   static constexpr uint32_t kTotal = kBars + 128 + 1024;
 };
+static_assert(StateSmemLayout::kSop % 1024 == 0 && StateSmemLayout::kOut % 1024 == 0,
+              "operand alignment");
 
-// TMEM columns: two [K;Q] S accumulators (alternate chunks, 64 each),
-// T [R_hi | R_lo] (M=64, 128), [0;P] v_new (64), K^T [Vd_hi | Vd_lo] (128).
-constexpr uint32_t kTmD1 = 0, kTmD3 = 128, kTmD4 = 256, kTmD5 = 320;
+// TMEM columns.  The S^T and v_new^T products use M=128 with the MN-major A
+// descriptor's LBO = 0, so both 64-row halves of the accumulator hold the
+// same 64 rows: all 128 lanes carry data and the register work of a phase
+// spreads over the four SM sub-partitions.
+//   D1[2] (0, 128): [S^T;S^T] [K;Q]^T, rows dv, cols 0-63 (K S)^T, 64-127 (Q S)^T
+//   D3 (256):       [T;T] [R_hi | R_lo] + [T_lo;T_lo] R_hi, rows tokens
+//   D4 (320):       [Vn^T;Vn^T] P^T = (P v_new)^T, rows dv; shares D3's
+//                   columns 64-127 once v_new has been read
+//   D5 (384):       K^T [Vd_hi | Vd_lo], rows dk
+constexpr uint32_t kTmD1 = 0, kTmD3 = 256, kTmD4 = 320, kTmD5 = 384;
 
-__device__ __forceinline__ void compute_barrier() {
-  asm volatile("bar.sync 1, 256;" ::: "memory");
+// Named barriers (288 threads each): the issuer arrives on kBarGoOut (the
+// previous chunk's output may be formed) and kBarGo (a product is ready) and
+// the compute warps wait; the compute warps arrive on kBarReady (operands
+// written) and the issuer waits.  Every two arrivals on one barrier are
+// separated by a wait of the arriving side on the other barrier, so no
+// arrival can fall into an earlier generation.
+constexpr int kBarGoOut = 1, kBarGo = 2, kBarReady = 3;
+
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src,
+                                             int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
 }
 
 __global__ void __launch_bounds__(kStateThreads, 1)
 gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
                        const __grid_constant__ CUtensorMap tm_v,
+                       const __grid_constant__ CUtensorMap tm_o,
                        const uint8_t* __restrict__ kq_records,
                        const uint8_t* __restrict__ records, float* __restrict__ state,
                        uint16_t* __restrict__ o_out, int qk_heads, int value_heads,
@@ -530,9 +570,14 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBars);
   uint64_t* smma = full + 2;       // per stage: the tensor core is done with it
   uint64_t* mma_bar = smma + 2;
-  uint64_t* fin_bar = mma_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin_bar + 1);
-  volatile uint32_t* wait_flags = tmem_slot + 1;  // two alternating slots
+  uint64_t* stage_free = mma_bar + 1;  // per stage: ready for the next load
+  uint64_t* tile_ready = stage_free + 2;  // per output tile: written, store it
+  uint64_t* tile_free = tile_ready + 2;   // per output tile: stored, reuse it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_free + 2);
+  // issuer -> compute: 1 = go on, 0 = stop; one word per go barrier
+  volatile uint32_t* flag_out = tmem_slot + 1;
+  volatile uint32_t* flag_go = tmem_slot + 2;
+  float* eg_prev = reinterpret_cast<float*>(smem + L::kEg);
 
   const int dvh = blockIdx.x;
   const int h = blockIdx.y;
@@ -545,69 +590,247 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
   const int seq_len = tab.cu[seq + 1] - seq_t0;
   const int nchunks = (seq_len + kChunk - 1) / kChunk;
   const int chunk0 = tab.chunk_start[seq];
+  const int last_n = seq_len - (nchunks - 1) * kChunk;   // tokens in the last chunk
 
-  // Stage loads: [K;Q] image and prep record (bulk copies), v (TMA).
-  auto load_stage = [&](int c) {
-    const int st = c & 1;
-    uint8_t* sb = smem + (st ? L::kStage1 : L::kStage0);
-    const int chunk = chunk0 + c;
-    mbar_arrive_expect_tx(&full[st], kStageTx);
-    bulk_load(sb + kStKQ, kq_records + (static_cast<int64_t>(chunk) * qk_heads + kh) * kKQBytes,
-              kKQBytes, &full[st]);
-    bulk_load(sb + kStRec, records + (static_cast<int64_t>(chunk) * value_heads + h) * kRecBytes,
-              kRecBytes, &full[st]);
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(sb + kStV)),
-        "l"(reinterpret_cast<uint64_t>(&tm_v)), "r"(smem_u32(&full[st])),
-        "r"(dvh * kDvHalf), "r"(h), "r"(seq_t0 + c * kChunk)
-        : "memory");
-  };
-  int issued = 0;    // chunks whose stage loads were issued (thread 0)
   if (tid == 0) {
     mbar_init(&full[0], 1);
     mbar_init(&full[1], 1);
     mbar_init(&smma[0], 1);
     mbar_init(&smma[1], 1);
     mbar_init(mma_bar, 1);
-    mbar_init(fin_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&stage_free[i], 1);
+      mbar_init(&tile_ready[i], 1);
+      mbar_init(&tile_free[i], 1);
+    }
     fence_barrier_init();
-    tma_prefetch_desc(&tm_v);
-    for (; issued < 2 && issued < nchunks; ++issued) load_stage(issued);
   }
   if (warp == 0) tmem_alloc(tmem_slot, 512);
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem = *tmem_slot;
+  uint8_t* sop = smem + L::kSop;
+  uint8_t* rimg = smem + L::kR;
+  uint8_t* vn = smem + L::kVn;
+  uint8_t* vdhi = smem + L::kVdhi;
+  uint8_t* vdlo = smem + L::kVdlo;
+  uint8_t* otile = smem + L::kOut;
 
-  {
-    // ---------------------------------------------------- compute warps --
+  if (warp == 8) {
+    // ======================================================= MMA issuer ==
+    const bool is0 = lane == 0;
+    // Lane 0 decides; the warp then signals the compute warps.
+    auto signal = [&](bool out, bool go) {
+      if (is0) *(out ? flag_out : flag_go) = go ? 1u : 0u;
+      __syncwarp();
+      named_arrive(out ? kBarGoOut : kBarGo, kSyncThreads);
+    };
+    auto bcast = [&](bool v) { return __shfl_sync(0xffffffffu, v ? 1 : 0, 0) != 0; };
+    bool ok = true;
+    uint32_t mma_phase = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int st = c & 1;
+      uint8_t* sb = smem + (st ? L::kStage1 : L::kStage0);
+      const uint32_t d1 = tmem + kTmD1 + (c & 1) * 128;
+      named_sync(kBarReady, kSyncThreads);        // S of this chunk written (and exp(G) saved)
+      // D1 = [S^T; S^T] [K;Q]^T (M=128 with LBO 0, N=128, K=128 dk), once
+      // the stage has landed.  Then: the stage of chunk c - 1 is free once its
+      // last MMA ((P v_new)^T) completed; the output tile of chunk c - 1 may be
+      // written once the store of chunk c - 3 (same buffer) has read it.
+      bool go = true;
+      if (is0) {
+        go = mbar_wait(&full[st], (c >> 1) & 1, err);
+        if (go) {
+          tmem_fence_after();
+          constexpr uint32_t id = umma_idesc_bf16(128, 128, true, false);
+          const uint32_t akq = smem_u32(sb + kStKQ);
+          const uint32_t as = smem_u32(sop);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(d1, umma_sdesc(as + kk * 2048u, 0, 1024),
+                      umma_sdesc(akq + (kk >> 2) * 16384u + (kk & 3) * 32u, 16, 1024), id,
+                      kk > 0 ? 1u : 0u);
+          umma_commit(mma_bar);
+          if (c >= 1) {
+            go = mbar_wait(&smma[st ^ 1], ((c - 1) >> 1) & 1, err);
+            if (go) mbar_arrive(&stage_free[st ^ 1]);
+          }
+          if (go && c >= 3) go = mbar_wait(&tile_free[(c - 1) & 1], ((c - 3) >> 1) & 1, err);
+        }
+      }
+      go = bcast(go);
+      signal(true, go);                           // compute: output of chunk c - 1
+      if (!go) { ok = false; break; }
+      if (is0) go = mbar_wait(mma_bar, mma_phase, err);
+      mma_phase ^= 1u;
+      go = bcast(go);
+      signal(false, go);                          // compute: R
+      if (!go) { ok = false; break; }
+
+      named_sync(kBarReady, kSyncThreads);        // R and the output tile written
+      if (is0) {
+        // D3[:, 0:64] = T_hi R_hi + T_lo R_hi, D3[:, 64:128] = T_hi R_lo
+        // (M=128 as [T;T] with LBO 0, B = R^T rows K-major).
+        tmem_fence_after();
+        constexpr uint32_t id_w = umma_idesc_bf16(128, 128, true, false);
+        constexpr uint32_t id_n = umma_idesc_bf16(128, 64, true, false);
+        const uint32_t thi = smem_u32(sb + kStRec + kRecTHi);
+        const uint32_t tlo = smem_u32(sb + kStRec + kRecTLo);
+        const uint32_t br = smem_u32(rimg);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16(tmem + kTmD3, umma_sdesc(thi + kk * 2048, 0, 1024),
+                    umma_sdesc(br + kk * 32, 16, 1024), id_w, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16(tmem + kTmD3, umma_sdesc(tlo + kk * 2048, 0, 1024),
+                    umma_sdesc(br + kk * 32, 16, 1024), id_n, 1u);
+        umma_commit(mma_bar);
+        if (c >= 1) mbar_arrive(&tile_ready[(c - 1) & 1]);
+        go = mbar_wait(mma_bar, mma_phase, err);
+      }
+      mma_phase ^= 1u;
+      go = bcast(go);
+      signal(false, go);                          // compute: v_new
+      if (!go) { ok = false; break; }
+
+      named_sync(kBarReady, kSyncThreads);        // Vn, Vd written
+      if (is0) {
+        // D5 = K^T [Vd_hi | Vd_lo]: the state chain.
+        tmem_fence_after();
+        constexpr uint32_t id_s = umma_idesc_bf16(128, 128, true, true);
+        const uint32_t akt = smem_u32(sb + kStKQ);
+        const uint32_t bd = smem_u32(vdhi);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          // A = K^T: MN-major view of the [K;Q] rows 0..63, dk slabs 16 KB apart.
+          umma_bf16(tmem + kTmD5, umma_sdesc(akt + kk * 2048, 16384, 1024),
+                    umma_sdesc(bd + kk * 2048, 8192, 1024), id_s, kk > 0 ? 1u : 0u);
+        umma_commit(mma_bar);
+        go = mbar_wait(mma_bar, mma_phase, err);
+      }
+      mma_phase ^= 1u;
+      go = bcast(go);
+      signal(false, go);                          // compute: state update
+      if (!go) { ok = false; break; }
+      // While the state update runs: D4 = [Vn^T; Vn^T] P^T = (P v_new)^T,
+      // completed behind a commit to the stage barrier.
+      if (is0) {
+        tmem_fence_after();
+        constexpr uint32_t id_o = umma_idesc_bf16(128, 64, true, false);
+        const uint32_t ap = smem_u32(sb + kStRec + kRecP);
+        const uint32_t bv = smem_u32(vn);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16(tmem + kTmD4, umma_sdesc(bv + kk * 2048, 0, 1024),
+                    umma_sdesc(ap + kk * 32, 16, 1024), id_o, kk > 0 ? 1u : 0u);
+        umma_commit(&smma[st]);
+      }
+    }
+    // Drain: every MMA issued (the last (P v_new)^T included) completes
+    // before the last output and the TMEM release.  After a failure the
+    // compute warps have left already and take no further handshake.
+    if (ok) named_sync(kBarReady, kSyncThreads);  // last state update done
+    bool drained = false;
+    if (is0) {
+      umma_commit(mma_bar);
+      drained = mbar_wait(mma_bar, mma_phase, err);
+      // The last tile's buffer: the store of chunk nchunks - 3 has read it.
+      if (drained && ok && nchunks >= 3 && last_n == kChunk)
+        drained = mbar_wait(&tile_free[(nchunks - 1) & 1], ((nchunks - 3) >> 1) & 1, err);
+    }
+    drained = bcast(drained);
+    if (ok) {
+      signal(false, drained);
+      named_sync(kBarReady, kSyncThreads);        // last output tile written
+      if (is0 && drained && nchunks > 0 && last_n == kChunk) mbar_arrive(&tile_ready[(nchunks - 1) & 1]);
+    }
+  } else if (warp == 9) {
+    // =========================================================== loader ==
+    // Stage loads, L2 prefetch and output stores, so that no copy issue sits
+    // in front of an MMA.
+    if (lane == 0) {
+      auto load_stage = [&](int c) {
+        const int st = c & 1;
+        uint8_t* sb = smem + (st ? L::kStage1 : L::kStage0);
+        const int chunk = chunk0 + c;
+        mbar_arrive_expect_tx(&full[st], kStageTx);
+        bulk_load(sb + kStKQ, kq_records + (static_cast<int64_t>(chunk) * qk_heads + kh) * kKQBytes,
+                  kKQBytes, &full[st]);
+        bulk_load(sb + kStRec, records + (static_cast<int64_t>(chunk) * value_heads + h) * kRecBytes,
+                  kRecBytes, &full[st]);
+        tma_load_3d(sb + kStV, &tm_v, &full[st], dvh * kDvHalf, h, seq_t0 + c * kChunk);
+      };
+      auto prefetch_stage = [&](int c) {
+        const int chunk = chunk0 + c;
+        prefetch_l2(kq_records + (static_cast<int64_t>(chunk) * qk_heads + kh) * kKQBytes, kKQBytes);
+        prefetch_l2(records + (static_cast<int64_t>(chunk) * value_heads + h) * kRecBytes, kRecBytes);
+        prefetch_l2_3d(&tm_v, dvh * kDvHalf, h, seq_t0 + c * kChunk);
+      };
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_o);
+      int issued = 0;
+      for (; issued < 2 && issued < nchunks; ++issued) load_stage(issued);
+      if (nchunks > 2) prefetch_stage(2);
+      bool ok = true;
+      for (int c = 1; c < nchunks && ok; ++c) {
+        // Chunk c + 1 into the stage chunk c - 1 used, once the MMA issuer
+        // saw that stage's last MMA complete (at its chunk c).
+        if (c + 1 < nchunks) {
+          ok = mbar_wait(&stage_free[(c + 1) & 1], ((c - 1) >> 1) & 1, err);
+          if (!ok) break;
+          load_stage(c + 1);
+          issued = c + 2;
+          if (c + 2 < nchunks) prefetch_stage(c + 2);
+        }
+        // The output tile of chunk c - 1, once written (after R of chunk c).
+        ok = mbar_wait(&tile_ready[(c - 1) & 1], ((c - 1) >> 1) & 1, err);
+        if (!ok) break;
+        tma_store_3d(&tm_o, otile + ((c - 1) & 1) * 8192, dvh * kDvHalf, h,
+                     seq_t0 + (c - 1) * kChunk);
+        bulk_commit();
+        if (c >= 2) {
+          bulk_wait_read<1>();                    // the store of chunk c - 2 has read its tile
+          mbar_arrive(&tile_free[(c - 2) & 1]);
+        }
+      }
+      // The last tile, when it is a full chunk (a shorter one was written
+      // row by row).
+      if (ok && nchunks > 0 && last_n == kChunk &&
+          mbar_wait(&tile_ready[(nchunks - 1) & 1], ((nchunks - 1) >> 1) & 1, err)) {
+        tma_store_3d(&tm_o, otile + ((nchunks - 1) & 1) * 8192, dvh * kDvHalf, h,
+                     seq_t0 + (nchunks - 1) * kChunk);
+        bulk_commit();
+      }
+      bulk_wait_all();
+      // Let stage copies still in flight land before exit (a completed
+      // phase returns at once).
+      for (int c = (issued > 2 ? issued - 2 : 0); c < issued; ++c) {
+        const unsigned long long t_start = global_ns();
+        while (!mbar_try_wait(&full[c & 1], (c >> 1) & 1) && global_ns() - t_start < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ============================================================ compute ==
     const float scale = 0.08838834764831845f;
-    const int cg = warp >> 2;             // column group: value columns [32 cg, 32 cg + 32)
-    const int quarter = warp & 3;         // TMEM lane quarter
-    const int lrow = quarter * 32 + lane; // TMEM lane of this thread
-    const int c0 = cg * kDvGroup;
-    const bool leader = tid == 0;         // issues every MMA
-    uint8_t* sop = smem + L::kSop;
-    uint8_t* rhi = smem + L::kRhi;
-    uint8_t* rlo = smem + L::kRlo;
-    uint8_t* vn = smem + L::kVn;
-    uint8_t* vdhi = smem + L::kVdhi;
-    uint8_t* vdlo = smem + L::kVdlo;
+    const int quarter = warp & 3;          // TMEM lane quarter
+    const int lrow = quarter * 32 + lane;  // TMEM lane of this thread
+    const int cg = warp >> 2;
+    const int c0 = cg * kDvGroup;          // state update: value columns [c0, c0 + 32)
+    const int half = lrow >> 6;            // which copy of a duplicated 64-row accumulator
+    const int r64 = lrow & 63;             // row inside it (dv or token)
+    const int seg = 32 * half + 16 * cg;   // the 16 columns this thread takes from it
 
-    // Bounded wait shared by the compute threads: the leader waits (only if
-    // `pre` holds) and the outcome reaches every compute thread through
-    // shared memory behind the compute barrier, so all take the same branch.
-    // Two flag slots alternate so a slot is rewritten only after a later
-    // barrier.
-    uint32_t nwaits = 0;
-    auto compute_wait = [&](uint64_t* bar, uint32_t parity, bool pre) -> bool {
-      volatile uint32_t* f = wait_flags + (nwaits & 1u);
-      ++nwaits;
-      if (leader) *f = (pre && mbar_wait(bar, parity, err)) ? 1u : 0u;
-      compute_barrier();
-      return *f != 0u;
+    auto wait_issuer = [&](bool out) -> bool {
+      named_sync(out ? kBarGoOut : kBarGo, kSyncThreads);
+      return *(out ? flag_out : flag_go) != 0u;
+    };
+    auto ready = [&]() {
+      fence_proxy_async_smem();
+      tmem_fence_before();
+      named_arrive(kBarReady, kSyncThreads);
     };
 
     // State: thread owns key row lrow, value columns dvh*64 + c0 + [0, 32).
@@ -628,207 +851,124 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
       }
     };
 
-    // Output rows of a finished chunk (lanes 64..127, row i = lrow - 64):
-    // O = scale (exp(G_i) (Q S)_i + (P v_new)_i).
-    int prev_t0 = 0, prev_n = 0;
-    float prev_eg = 0.f;
-    auto write_output = [&](uint32_t d1) {
-      const int i = lrow - 64;
-      uint32_t rq[2][16], rp[2][16];
-      tmem_ld16(tmem_addr(d1, quarter * 32, c0), rq[0]);
-      tmem_ld16(tmem_addr(d1, quarter * 32, c0 + 16), rq[1]);
-      tmem_ld16(tmem_addr(tmem + kTmD4, quarter * 32, c0), rp[0]);
-      tmem_ld16(tmem_addr(tmem + kTmD4, quarter * 32, c0 + 16), rp[1]);
+    // Output of a finished chunk, transposed: this thread has value column
+    // d = r64 and tokens [seg, seg + 16): O = scale (exp(G) (Q S) + P v_new),
+    // into the 128-byte-swizzled tile (a TMA store writes it out) or, for a
+    // last chunk shorter than 64 tokens, straight to its rows.
+    int prev_t0 = 0;
+    auto write_output = [&](uint32_t d1, int buf, int rows) {
+      uint32_t rq[16], rp[16];
+      tmem_ld16(tmem_addr(d1, quarter * 32, 64 + seg), rq);
+      tmem_ld16(tmem_addr(tmem + kTmD4, quarter * 32, seg), rp);
+      float eg[16];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const float4 e4 = *reinterpret_cast<const float4*>(eg_prev + seg + 4 * q4);
+        eg[4 * q4] = e4.x; eg[4 * q4 + 1] = e4.y; eg[4 * q4 + 2] = e4.z; eg[4 * q4 + 3] = e4.w;
+      }
       tmem_ld_wait();
-      if (i < prev_n) {
-        uint16_t* orow = o_out + (static_cast<int64_t>(prev_t0 + i) * value_heads + h) * kHeadDim +
-                         dvh * kDvHalf + c0;
-        uint32_t w[16];
+      if (rows == kChunk) {
+        uint8_t* tile = otile + buf * 8192;
 #pragma unroll
-        for (int p = 0; p < 16; ++p) {
-          const int e = 2 * p;
-          const float o0 = scale * (prev_eg * __uint_as_float(rq[e >> 4][e & 15]) + __uint_as_float(rp[e >> 4][e & 15]));
-          const float o1 = scale * (prev_eg * __uint_as_float(rq[e >> 4][(e & 15) + 1]) + __uint_as_float(rp[e >> 4][(e & 15) + 1]));
-          w[p] = pack_bf16x2(o0, o1);
+        for (int t = 0; t < 16; ++t) {
+          const float o = scale * (eg[t] * __uint_as_float(rq[t]) + __uint_as_float(rp[t]));
+          *reinterpret_cast<uint16_t*>(tile + sw128_chunk(seg + t, r64 >> 3) + (r64 & 7) * 2) =
+              f32_to_bf16_bits(o);
         }
+      } else {
+        uint16_t* ocol = o_out + (static_cast<int64_t>(prev_t0 + seg) * value_heads + h) * kHeadDim +
+                         dvh * kDvHalf + r64;
+        const int64_t tstride = static_cast<int64_t>(value_heads) * kHeadDim;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          reinterpret_cast<uint4*>(orow)[q4] = make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+        for (int t = 0; t < 16; ++t) {
+          if (seg + t < rows) {
+            const float o = scale * (eg[t] * __uint_as_float(rq[t]) + __uint_as_float(rp[t]));
+            ocol[t * tstride] = f32_to_bf16_bits(o);
+          }
+        }
       }
     };
 
     write_sop();
-    // Zero blocks in front of P in both stages (never written by the loader).
-    for (int e = tid; e < 2 * 8192 / 16; e += 256) {
-      const int st = e / 512;
-      reinterpret_cast<uint4*>(smem + (st ? L::kStage1 : L::kStage0) + kStZero)[e % 512] =
-          make_uint4(0u, 0u, 0u, 0u);
-    }
-    fence_proxy_async_smem();
-    compute_barrier();
-
-    uint32_t mma_phase = 0;
+    ready();                                   // S of chunk 0 written
     bool ok = true;
-    bool lead_ok = true;   // thread 0: every wait of its own succeeded
-    int consumed = 0;      // chunks whose stage was seen landed
     for (int c = 0; c < nchunks; ++c) {
       const int st = c & 1;
       uint8_t* sb = smem + (st ? L::kStage1 : L::kStage0);
       const float* fac = reinterpret_cast<const float*>(sb + kStRec + kRecF);
-      const int t0 = seq_t0 + c * kChunk;
-      const int n = min(kChunk, seq_t0 + seq_len - t0);
-      const uint32_t d1 = tmem + kTmD1 + (c & 1) * 64;
-      const uint32_t d1_prev = tmem + kTmD1 + ((c & 1) ^ 1) * 64;
+      const uint32_t d1 = tmem + kTmD1 + (c & 1) * 128;
+      const uint32_t d1_prev = tmem + kTmD1 + ((c & 1) ^ 1) * 128;
 
-      // D1 = [K;Q] S  (M=128, N=64, K=128; S as MN-major B), once the stage
-      // has landed.
-      bool landed = lead_ok;
-      if (leader && landed) {
-        landed = mbar_wait(&full[st], (c >> 1) & 1, err);
-        if (landed) {
-          tmem_fence_after();
-          constexpr uint32_t id = umma_idesc_bf16(128, 64, false, true);
-          const uint32_t akq = smem_u32(sb + kStKQ);
-          const uint32_t bs = smem_u32(sop);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            umma_bf16(d1, umma_sdesc(akq + (kk >> 2) * 16384u + (kk & 3) * 32u, 16, 1024),
-                      umma_sdesc(bs + kk * 2048u, 16384, 1024), id, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(mma_bar);
-          // The stage of chunk c - 1 takes chunk c + 1 once the MMAs reading
-          // it have completed (every thread finished with it at the end of
-          // chunk c - 1); done here, while the MMAs above run.
-          if (c >= 1 && c + 1 < nchunks) {
-            lead_ok = mbar_wait(&smma[st ^ 1], ((c - 1) >> 1) & 1, err);
-            if (lead_ok) {
-              load_stage(c + 1);
-              issued = c + 2;
-            }
-            landed = lead_ok;
-          }
-        }
-      }
-      // Completion of this commit also covers the previous chunk's [0;P] v_new.
-      if (!compute_wait(mma_bar, mma_phase, landed)) { ok = false; break; }
-      consumed = c + 1;
-      mma_phase ^= 1u;
+      if (!wait_issuer(true)) { ok = false; break; }   // stage landed, D1 issued, (P v_new)^T done
+      tmem_fence_after();
+      if (c > 0) write_output(d1_prev, (c - 1) & 1, kChunk);
+      if (!wait_issuer(false)) { ok = false; break; }  // D1 complete
       tmem_fence_after();
 
-      if (quarter < 2) {
-        // R = beta V - beta exp(G) (K S) for token rows (lanes 0-63).
-        const int i = lrow;
-        uint32_t r[2][16];
-        tmem_ld16(tmem_addr(d1, quarter * 32, c0), r[0]);
-        tmem_ld16(tmem_addr(d1, quarter * 32, c0 + 16), r[1]);
-        const float bi = fac[kFBeta + i], begi = fac[kFBetaEG + i];
-        uint4 vv[4];
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          vv[q4] = *reinterpret_cast<const uint4*>(sb + kStV + sw128_chunk(i, (c0 >> 3) + q4));
-        tmem_ld_wait();
+      // R^T = (beta V - beta exp(G) (K S))^T, hi/lo, for value column d = r64
+      // and tokens [seg, seg + 16): K-major rows d (hi) and 64 + d (lo).
+      {
+        uint32_t rk[16];
+        tmem_ld16(tmem_addr(d1, quarter * 32, seg), rk);
+        float bv[16], bg[16];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          const uint32_t vw[4] = {vv[q4].x, vv[q4].y, vv[q4].z, vv[q4].w};
-          uint32_t hi[4], lo[4];
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            const int e = 8 * q4 + 2 * p;
-            const float r0 = bi * bf16lo_f32(vw[p]) - begi * __uint_as_float(r[e >> 4][e & 15]);
-            const float r1 = bi * bf16hi_f32(vw[p]) - begi * __uint_as_float(r[e >> 4][(e & 15) + 1]);
-            split_bf16x2(r0, r1, hi[p], lo[p]);
-          }
-          const uint32_t off = sw128_chunk(i, (c0 >> 3) + q4);
-          *reinterpret_cast<uint4*>(rhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-          *reinterpret_cast<uint4*>(rlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          const float4 b4 = *reinterpret_cast<const float4*>(fac + kFBeta + seg + 4 * q4);
+          const float4 g4 = *reinterpret_cast<const float4*>(fac + kFBetaEG + seg + 4 * q4);
+          bv[4 * q4] = b4.x; bv[4 * q4 + 1] = b4.y; bv[4 * q4 + 2] = b4.z; bv[4 * q4 + 3] = b4.w;
+          bg[4 * q4] = g4.x; bg[4 * q4 + 1] = g4.y; bg[4 * q4 + 2] = g4.z; bg[4 * q4 + 3] = g4.w;
         }
-      } else if (c > 0) {
-        write_output(d1_prev);   // previous chunk, off the state chain
-      }
-      fence_proxy_async_smem();
-      tmem_fence_before();
-      compute_barrier();
-
-      // D3[:, 0:64] = T_hi R_hi + T_lo R_hi, D3[:, 64:128] = T_hi R_lo
-      // (M=64, A MN-major); v_new = D3[:, j] + D3[:, 64 + j].
-      if (leader) {
-        tmem_fence_after();
-        constexpr uint32_t id_w = umma_idesc_bf16(64, 128, true, true);
-        constexpr uint32_t id_n = umma_idesc_bf16(64, 64, true, true);
-        const uint32_t thi = smem_u32(sb + kStRec + kRecTHi);
-        const uint32_t tlo = smem_u32(sb + kStRec + kRecTLo);
-        const uint32_t br = smem_u32(rhi);
+        float vv[16];
+        const uint8_t* vt = sb + kStV;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem + kTmD3, umma_sdesc(thi + kk * 2048, 8192, 1024),
-                    umma_sdesc(br + kk * 2048, 8192, 1024), id_w, kk > 0 ? 1u : 0u);
+        for (int t = 0; t < 16; ++t)
+          vv[t] = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
+              vt + sw128_chunk(seg + t, r64 >> 3) + (r64 & 7) * 2));
+        tmem_ld_wait();
+        uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem + kTmD3, umma_sdesc(tlo + kk * 2048, 8192, 1024),
-                    umma_sdesc(br + kk * 2048, 8192, 1024), id_n, 1u);
-        umma_commit(mma_bar);
+        for (int p = 0; p < 8; ++p) {
+          const float x0 = bv[2 * p] * vv[2 * p] - bg[2 * p] * __uint_as_float(rk[2 * p]);
+          const float x1 = bv[2 * p + 1] * vv[2 * p + 1] - bg[2 * p + 1] * __uint_as_float(rk[2 * p + 1]);
+          split_bf16x2(x0, x1, hi[p], lo[p]);
+        }
+        const int ch = seg >> 3;
+        *reinterpret_cast<uint4*>(rimg + sw128_chunk(r64, ch)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(rimg + sw128_chunk(r64, ch + 1)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+        *reinterpret_cast<uint4*>(rimg + 8192 + sw128_chunk(r64, ch)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(rimg + 8192 + sw128_chunk(r64, ch + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
       }
-      if (!compute_wait(mma_bar, mma_phase, true)) { ok = false; break; }
-      mma_phase ^= 1u;
+      ready();
+      if (!wait_issuer(false)) { ok = false; break; }  // D3 complete
       tmem_fence_after();
 
-      // v_new rows (M=64 layout: row 16*quarter + lane, lane < 16): bf16
-      // v_new, and v_new exp(G_C - G) as a hi/lo pair.
+      // v_new for token i = r64 and value columns [seg, seg + 16): bf16 v_new
+      // and v_new exp(G_C - G) as a hi/lo pair (MN-major rows i).
       {
-        const int i = quarter * 16 + lane;
-        uint32_t ra[2][16], rb[2][16];
-        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, c0), ra[0]);
-        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, c0 + 16), ra[1]);
-        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, 64 + c0), rb[0]);
-        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, 64 + c0 + 16), rb[1]);
-        const float edi = (lane < 16) ? fac[kFED + i] : 0.f;
+        uint32_t ra[16], rb[16];
+        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, seg), ra);
+        tmem_ld16(tmem_addr(tmem + kTmD3, quarter * 32, 64 + seg), rb);
+        const float edi = fac[kFED + r64];
         tmem_ld_wait();
-        if (lane < 16) {
+        uint32_t vb[8], dh[8], dl[8];
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint32_t vb[4], dh[4], dl[4];
+        for (int p = 0; p < 8; ++p) {
+          const float v0 = __uint_as_float(ra[2 * p]) + __uint_as_float(rb[2 * p]);
+          const float v1 = __uint_as_float(ra[2 * p + 1]) + __uint_as_float(rb[2 * p + 1]);
+          vb[p] = pack_bf16x2(v0, v1);
+          split_bf16x2(v0 * edi, v1 * edi, dh[p], dl[p]);
+        }
+        const int ch = seg >> 3;
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
-              const int e = 8 * q4 + 2 * p;
-              const float v0 = __uint_as_float(ra[e >> 4][e & 15]) + __uint_as_float(rb[e >> 4][e & 15]);
-              const float v1 = __uint_as_float(ra[e >> 4][(e & 15) + 1]) + __uint_as_float(rb[e >> 4][(e & 15) + 1]);
-              vb[p] = pack_bf16x2(v0, v1);
-              split_bf16x2(v0 * edi, v1 * edi, dh[p], dl[p]);
-            }
-            const uint32_t off = sw128_chunk(i, (c0 >> 3) + q4);
-            *reinterpret_cast<uint4*>(vn + off) = make_uint4(vb[0], vb[1], vb[2], vb[3]);
-            *reinterpret_cast<uint4*>(vdhi + off) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
-            *reinterpret_cast<uint4*>(vdlo + off) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
-          }
+        for (int k2 = 0; k2 < 2; ++k2) {
+          const uint32_t off = sw128_chunk(r64, ch + k2);
+          *reinterpret_cast<uint4*>(vn + off) = make_uint4(vb[4 * k2], vb[4 * k2 + 1], vb[4 * k2 + 2], vb[4 * k2 + 3]);
+          *reinterpret_cast<uint4*>(vdhi + off) = make_uint4(dh[4 * k2], dh[4 * k2 + 1], dh[4 * k2 + 2], dh[4 * k2 + 3]);
+          *reinterpret_cast<uint4*>(vdlo + off) = make_uint4(dl[4 * k2], dl[4 * k2 + 1], dl[4 * k2 + 2], dl[4 * k2 + 3]);
         }
       }
-      fence_proxy_async_smem();
-      tmem_fence_before();
-      compute_barrier();
-
-      // D5 = K^T [Vd_hi | Vd_lo] (M=128, N=128, A MN-major): the state chain.
-      // Then D4 = [0;P] v_new for the output, completed behind the next commit.
-      if (leader) {
-        tmem_fence_after();
-        constexpr uint32_t id_s = umma_idesc_bf16(128, 128, true, true);
-        constexpr uint32_t id_o = umma_idesc_bf16(128, 64, false, true);
-        const uint32_t akt = smem_u32(sb + kStKQ);
-        const uint32_t ap = smem_u32(sb + kStZero);
-        const uint32_t bv = smem_u32(vn), bd = smem_u32(vdhi);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          // A = K^T: MN-major view of the [K;Q] rows 0..63, dk slabs 16 KB apart.
-          umma_bf16(tmem + kTmD5, umma_sdesc(akt + kk * 2048, 16384, 1024),
-                    umma_sdesc(bd + kk * 2048, 8192, 1024), id_s, kk > 0 ? 1u : 0u);
-        umma_commit(mma_bar);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem + kTmD4, umma_sdesc(ap + kk * 32, 16, 1024),
-                    umma_sdesc(bv + kk * 2048, 8192, 1024), id_o, kk > 0 ? 1u : 0u);
-        umma_commit(&smma[st]);    // every MMA reading this stage has completed
-      }
-      if (!compute_wait(mma_bar, mma_phase, true)) { ok = false; break; }
-      mma_phase ^= 1u;
+      ready();
+      if (!wait_issuer(false)) { ok = false; break; }  // D5 complete
       tmem_fence_after();
 
       // State update (every lane): S = exp(G_C) S + K^T Vd_hi + K^T Vd_lo.
@@ -839,36 +979,25 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
         tmem_ld16(tmem_addr(tmem + kTmD5, quarter * 32, 64 + c0), rb[0]);
         tmem_ld16(tmem_addr(tmem + kTmD5, quarter * 32, 64 + c0 + 16), rb[1]);
         const float dl = fac[kFELast];
-        if (quarter >= 2) prev_eg = fac[kFEG + lrow - 64];
+        if (tid < 64) eg_prev[tid] = fac[kFEG + tid];
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < kDvGroup; ++j)
           s[j] = dl * s[j] + (__uint_as_float(ra[j >> 4][j & 15]) + __uint_as_float(rb[j >> 4][j & 15]));
         write_sop();
       }
-      prev_t0 = t0;
-      prev_n = n;
-      fence_proxy_async_smem();
-      tmem_fence_before();
-      compute_barrier();
+      prev_t0 = seq_t0 + c * kChunk;
+      ready();
     }
-    // Drain: every MMA issued (the last [0;P] v_new included) completes
-    // before the last output, the state write and the TMEM release.
-    if (leader) umma_commit(fin_bar);
-    const bool drained = compute_wait(fin_bar, 0, true);
-    if (ok && drained) {
-      tmem_fence_after();
-      if (quarter >= 2 && nchunks > 0) write_output(tmem + kTmD1 + ((nchunks - 1) & 1) * 64);
+    // The issuer drains the tensor core, then the last output and the state.
+    if (ok) {
+      if (wait_issuer(false)) {
+        tmem_fence_after();
+        if (nchunks > 0) write_output(tmem + kTmD1 + ((nchunks - 1) & 1) * 128, (nchunks - 1) & 1, last_n);
 #pragma unroll
-      for (int j = 0; j < kDvGroup; ++j) sg[(dvh * kDvHalf + c0 + j) * kHeadDim + lrow] = s[j];
-    }
-    // After a failure, let stage copies still in flight land before exit.
-    if (leader && !ok) {
-      for (int c = consumed; c < issued; ++c) {
-        const unsigned long long t_start = global_ns();
-        while (!mbar_try_wait(&full[c & 1], (c >> 1) & 1) && global_ns() - t_start < kWaitLimitNs) {
-        }
+        for (int j = 0; j < kDvGroup; ++j) sg[(dvh * kDvHalf + c0 + j) * kHeadDim + lrow] = s[j];
       }
+      ready();
     }
   }
   tmem_fence_before();
@@ -980,8 +1109,10 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
                            st_smem);
   if (e != cudaSuccess) return e;
   dim3 sgrid(kHeadDim / kDvHalf, value_heads, tab.num_seqs);
+  CUtensorMap to;
+  if (!make_tmap_thd(&to, o_out, tokens, value_heads)) return cudaErrorInvalidValue;
   gdn_chunk_state_kernel<<<sgrid, kStateThreads, st_smem, stream>>>(
-      tab, tv, kq_records, records, state, o_out, qk_heads, value_heads, err);
+      tab, tv, to, kq_records, records, state, o_out, qk_heads, value_heads, err);
   return cudaGetLastError();
 }
 

@@ -171,6 +171,21 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Prefetch into L2 (no shared memory involved): a byte range, or a tensor
+// box.  Sizes are multiples of 16 bytes.
+__device__ __forceinline__ void prefetch_l2(const void* gmem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gmem)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void prefetch_l2_3d(const CUtensorMap* map, int32_t c0, int32_t c1,
+                                               int32_t c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
 // 1-D bulk copy shared -> global, tracked by the issuing thread's bulk
 // groups.  Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
