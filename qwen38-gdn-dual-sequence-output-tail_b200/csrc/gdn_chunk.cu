@@ -476,14 +476,13 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
 
 // =========================================================== state =====
 
-// Eight compute warps, an MMA issuer warp and a loader warp.  Lane 0 of
-// warp 8 issues every MMA and waits on the tensor core; compute warps and
-// issuer hand over through named barriers (compute -> issuer: operands
-// ready; issuer -> compute: products ready, with an ok flag).  Lane 0 of
-// warp 9 issues the stage loads, the L2 prefetch and the output stores,
-// driven by mbarriers from the issuer.
+// Eight compute warps, an MMA issuer warp and a loader warp, handing over
+// through mbarriers only (every wait bounded): the compute warps arrive on
+// `rdy` when a phase's operands are written and wait on the tensor core's
+// commit barrier themselves; lane 0 of warp 8 waits on `rdy` and issues the
+// MMAs; lane 0 of warp 9 issues the stage loads, the L2 prefetch and the
+// output stores.
 constexpr int kStateThreads = 320;
-constexpr int kSyncThreads = 288;       // compute warps + MMA issuer warp
 constexpr int kComputeThreads = 256;
 constexpr int kDvHalf = 64;         // value columns per CTA
 constexpr int kDvGroup = 32;        // value columns per thread in the state update
@@ -531,20 +530,6 @@ static_assert(StateSmemLayout::kSop % 1024 == 0 && StateSmemLayout::kOut % 1024 
 //   D5 (384):       K^T [Vd_hi | Vd_lo], rows dk
 constexpr uint32_t kTmD1 = 0, kTmD3 = 256, kTmD4 = 320, kTmD5 = 384;
 
-// Named barriers (288 threads each): the issuer arrives on kBarGoOut (the
-// previous chunk's output may be formed) and kBarGo (a product is ready) and
-// the compute warps wait; the compute warps arrive on kBarReady (operands
-// written) and the issuer waits.  Every two arrivals on one barrier are
-// separated by a wait of the arriving side on the other barrier, so no
-// arrival can fall into an earlier generation.
-constexpr int kBarGoOut = 1, kBarGo = 2, kBarReady = 3;
-
-__device__ __forceinline__ void named_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-__device__ __forceinline__ void named_arrive(int id, int n) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src,
                                              int32_t c0, int32_t c1, int32_t c2) {
@@ -573,10 +558,8 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
   uint64_t* stage_free = mma_bar + 1;  // per stage: ready for the next load
   uint64_t* tile_ready = stage_free + 2;  // per output tile: written, store it
   uint64_t* tile_free = tile_ready + 2;   // per output tile: stored, reuse it
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_free + 2);
-  // issuer -> compute: 1 = go on, 0 = stop; one word per go barrier
-  volatile uint32_t* flag_out = tmem_slot + 1;
-  volatile uint32_t* flag_go = tmem_slot + 2;
+  uint64_t* rdy = tile_free + 2;          // compute -> issuer: operands written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rdy + 1);
   float* eg_prev = reinterpret_cast<float*>(smem + L::kEg);
 
   const int dvh = blockIdx.x;
@@ -600,9 +583,10 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
     mbar_init(mma_bar, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&stage_free[i], 1);
-      mbar_init(&tile_ready[i], 1);
+      mbar_init(&tile_ready[i], kComputeThreads);
       mbar_init(&tile_free[i], 1);
     }
+    mbar_init(rdy, kComputeThreads);
     fence_barrier_init();
   }
   if (warp == 0) tmem_alloc(tmem_slot, 512);
@@ -619,30 +603,23 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
 
   if (warp == 8) {
     // ======================================================= MMA issuer ==
-    const bool is0 = lane == 0;
-    // Lane 0 decides; the warp then signals the compute warps.
-    auto signal = [&](bool out, bool go) {
-      if (is0) *(out ? flag_out : flag_go) = go ? 1u : 0u;
-      __syncwarp();
-      named_arrive(out ? kBarGoOut : kBarGo, kSyncThreads);
-    };
-    auto bcast = [&](bool v) { return __shfl_sync(0xffffffffu, v ? 1 : 0, 0) != 0; };
-    bool ok = true;
-    uint32_t mma_phase = 0;
-    for (int c = 0; c < nchunks; ++c) {
-      const int st = c & 1;
-      uint8_t* sb = smem + (st ? L::kStage1 : L::kStage0);
-      const uint32_t d1 = tmem + kTmD1 + (c & 1) * 128;
-      named_sync(kBarReady, kSyncThreads);        // S of this chunk written (and exp(G) saved)
-      // D1 = [S^T; S^T] [K;Q]^T (M=128 with LBO 0, N=128, K=128 dk), once
-      // the stage has landed.  Then: the stage of chunk c - 1 is free once its
-      // last MMA ((P v_new)^T) completed; the output tile of chunk c - 1 may be
-      // written once the store of chunk c - 3 (same buffer) has read it.
-      bool go = true;
-      if (is0) {
-        go = mbar_wait(&full[st], (c >> 1) & 1, err);
-        if (go) {
-          tmem_fence_after();
+    if (lane == 0) {
+      uint32_t rdy_phase = 0;
+      auto wait_rdy = [&]() -> bool {
+        const bool r = mbar_wait(rdy, rdy_phase, err);
+        rdy_phase ^= 1u;
+        tmem_fence_after();
+        return r;
+      };
+      bool ok = true;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int st = c & 1;
+        uint8_t* sb = smem + (st ? L::kStage1 : L::kStage0);
+        const uint32_t d1 = tmem + kTmD1 + (c & 1) * 128;
+        // D1 = [S^T; S^T] [K;Q]^T (M=128 with LBO 0, N=128, K=128 dk), once S
+        // of this chunk is written and the stage has landed.
+        if (!(ok = wait_rdy() && mbar_wait(&full[st], (c >> 1) & 1, err))) break;
+        {
           constexpr uint32_t id = umma_idesc_bf16(128, 128, true, false);
           const uint32_t akq = smem_u32(sb + kStKQ);
           const uint32_t as = smem_u32(sop);
@@ -652,99 +629,58 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
                       umma_sdesc(akq + (kk >> 2) * 16384u + (kk & 3) * 32u, 16, 1024), id,
                       kk > 0 ? 1u : 0u);
           umma_commit(mma_bar);
-          if (c >= 1) {
-            go = mbar_wait(&smma[st ^ 1], ((c - 1) >> 1) & 1, err);
-            if (go) mbar_arrive(&stage_free[st ^ 1]);
-          }
-          if (go && c >= 3) go = mbar_wait(&tile_free[(c - 1) & 1], ((c - 3) >> 1) & 1, err);
         }
-      }
-      go = bcast(go);
-      signal(true, go);                           // compute: output of chunk c - 1
-      if (!go) { ok = false; break; }
-      if (is0) go = mbar_wait(mma_bar, mma_phase, err);
-      mma_phase ^= 1u;
-      go = bcast(go);
-      signal(false, go);                          // compute: R
-      if (!go) { ok = false; break; }
-
-      named_sync(kBarReady, kSyncThreads);        // R and the output tile written
-      if (is0) {
+        // The stage of chunk c - 1 takes chunk c + 1 once its last MMA
+        // ((P v_new)^T) completed (every thread finished with it: the rdy of
+        // the state update above).
+        if (c >= 1) {
+          if (!(ok = mbar_wait(&smma[st ^ 1], ((c - 1) >> 1) & 1, err))) break;
+          mbar_arrive(&stage_free[st ^ 1]);
+        }
         // D3[:, 0:64] = T_hi R_hi + T_lo R_hi, D3[:, 64:128] = T_hi R_lo
         // (M=128 as [T;T] with LBO 0, B = R^T rows K-major).
-        tmem_fence_after();
-        constexpr uint32_t id_w = umma_idesc_bf16(128, 128, true, false);
-        constexpr uint32_t id_n = umma_idesc_bf16(128, 64, true, false);
-        const uint32_t thi = smem_u32(sb + kStRec + kRecTHi);
-        const uint32_t tlo = smem_u32(sb + kStRec + kRecTLo);
-        const uint32_t br = smem_u32(rimg);
+        if (!(ok = wait_rdy())) break;
+        {
+          constexpr uint32_t id_w = umma_idesc_bf16(128, 128, true, false);
+          constexpr uint32_t id_n = umma_idesc_bf16(128, 64, true, false);
+          const uint32_t thi = smem_u32(sb + kStRec + kRecTHi);
+          const uint32_t tlo = smem_u32(sb + kStRec + kRecTLo);
+          const uint32_t br = smem_u32(rimg);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem + kTmD3, umma_sdesc(thi + kk * 2048, 0, 1024),
-                    umma_sdesc(br + kk * 32, 16, 1024), id_w, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + kTmD3, umma_sdesc(thi + kk * 2048, 0, 1024),
+                      umma_sdesc(br + kk * 32, 16, 1024), id_w, kk > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem + kTmD3, umma_sdesc(tlo + kk * 2048, 0, 1024),
-                    umma_sdesc(br + kk * 32, 16, 1024), id_n, 1u);
-        umma_commit(mma_bar);
-        if (c >= 1) mbar_arrive(&tile_ready[(c - 1) & 1]);
-        go = mbar_wait(mma_bar, mma_phase, err);
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + kTmD3, umma_sdesc(tlo + kk * 2048, 0, 1024),
+                      umma_sdesc(br + kk * 32, 16, 1024), id_n, 1u);
+          umma_commit(mma_bar);
+        }
+        // D5 = K^T [Vd_hi | Vd_lo] (the state chain), then D4 = [Vn^T; Vn^T]
+        // P^T = (P v_new)^T, completed behind a commit to the stage barrier.
+        if (!(ok = wait_rdy())) break;
+        {
+          constexpr uint32_t id_s = umma_idesc_bf16(128, 128, true, true);
+          constexpr uint32_t id_o = umma_idesc_bf16(128, 64, true, false);
+          const uint32_t akt = smem_u32(sb + kStKQ);
+          const uint32_t ap = smem_u32(sb + kStRec + kRecP);
+          const uint32_t bv = smem_u32(vn), bd = smem_u32(vdhi);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            // A = K^T: MN-major view of the [K;Q] rows 0..63, dk slabs 16 KB apart.
+            umma_bf16(tmem + kTmD5, umma_sdesc(akt + kk * 2048, 16384, 1024),
+                      umma_sdesc(bd + kk * 2048, 8192, 1024), id_s, kk > 0 ? 1u : 0u);
+          umma_commit(mma_bar);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + kTmD4, umma_sdesc(bv + kk * 2048, 0, 1024),
+                      umma_sdesc(ap + kk * 32, 16, 1024), id_o, kk > 0 ? 1u : 0u);
+          umma_commit(&smma[st]);
+        }
       }
-      mma_phase ^= 1u;
-      go = bcast(go);
-      signal(false, go);                          // compute: v_new
-      if (!go) { ok = false; break; }
-
-      named_sync(kBarReady, kSyncThreads);        // Vn, Vd written
-      if (is0) {
-        // D5 = K^T [Vd_hi | Vd_lo]: the state chain.
-        tmem_fence_after();
-        constexpr uint32_t id_s = umma_idesc_bf16(128, 128, true, true);
-        const uint32_t akt = smem_u32(sb + kStKQ);
-        const uint32_t bd = smem_u32(vdhi);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          // A = K^T: MN-major view of the [K;Q] rows 0..63, dk slabs 16 KB apart.
-          umma_bf16(tmem + kTmD5, umma_sdesc(akt + kk * 2048, 16384, 1024),
-                    umma_sdesc(bd + kk * 2048, 8192, 1024), id_s, kk > 0 ? 1u : 0u);
-        umma_commit(mma_bar);
-        go = mbar_wait(mma_bar, mma_phase, err);
-      }
-      mma_phase ^= 1u;
-      go = bcast(go);
-      signal(false, go);                          // compute: state update
-      if (!go) { ok = false; break; }
-      // While the state update runs: D4 = [Vn^T; Vn^T] P^T = (P v_new)^T,
-      // completed behind a commit to the stage barrier.
-      if (is0) {
-        tmem_fence_after();
-        constexpr uint32_t id_o = umma_idesc_bf16(128, 64, true, false);
-        const uint32_t ap = smem_u32(sb + kStRec + kRecP);
-        const uint32_t bv = smem_u32(vn);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem + kTmD4, umma_sdesc(bv + kk * 2048, 0, 1024),
-                    umma_sdesc(ap + kk * 32, 16, 1024), id_o, kk > 0 ? 1u : 0u);
-        umma_commit(&smma[st]);
-      }
-    }
-    // Drain: every MMA issued (the last (P v_new)^T included) completes
-    // before the last output and the TMEM release.  After a failure the
-    // compute warps have left already and take no further handshake.
-    if (ok) named_sync(kBarReady, kSyncThreads);  // last state update done
-    bool drained = false;
-    if (is0) {
+      // Drain: every MMA issued completes before TMEM is released (the
+      // compute warps wait on the same commit before the last output).
       umma_commit(mma_bar);
-      drained = mbar_wait(mma_bar, mma_phase, err);
-      // The last tile's buffer: the store of chunk nchunks - 3 has read it.
-      if (drained && ok && nchunks >= 3 && last_n == kChunk)
-        drained = mbar_wait(&tile_free[(nchunks - 1) & 1], ((nchunks - 3) >> 1) & 1, err);
-    }
-    drained = bcast(drained);
-    if (ok) {
-      signal(false, drained);
-      named_sync(kBarReady, kSyncThreads);        // last output tile written
-      if (is0 && drained && nchunks > 0 && last_n == kChunk) mbar_arrive(&tile_ready[(nchunks - 1) & 1]);
     }
   } else if (warp == 9) {
     // =========================================================== loader ==
@@ -823,14 +759,17 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
     const int r64 = lrow & 63;             // row inside it (dv or token)
     const int seg = 32 * half + 16 * cg;   // the 16 columns this thread takes from it
 
-    auto wait_issuer = [&](bool out) -> bool {
-      named_sync(out ? kBarGoOut : kBarGo, kSyncThreads);
-      return *(out ? flag_out : flag_go) != 0u;
+    uint32_t mma_phase = 0;
+    auto wait_mma = [&]() -> bool {
+      const bool r = mbar_wait(mma_bar, mma_phase, err);
+      mma_phase ^= 1u;
+      tmem_fence_after();
+      return r;
     };
     auto ready = [&]() {
       fence_proxy_async_smem();
       tmem_fence_before();
-      named_arrive(kBarReady, kSyncThreads);
+      mbar_arrive(rdy);
     };
 
     // State: thread owns key row lrow, value columns dvh*64 + c0 + [0, 32).
@@ -899,11 +838,23 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
       const uint32_t d1 = tmem + kTmD1 + (c & 1) * 128;
       const uint32_t d1_prev = tmem + kTmD1 + ((c & 1) ^ 1) * 128;
 
-      if (!wait_issuer(true)) { ok = false; break; }   // stage landed, D1 issued, (P v_new)^T done
-      tmem_fence_after();
-      if (c > 0) write_output(d1_prev, (c - 1) & 1, kChunk);
-      if (!wait_issuer(false)) { ok = false; break; }  // D1 complete
-      tmem_fence_after();
+      // Output of chunk c - 1 while D1 forms: every thread's state update of
+      // chunk c - 1 is done (exp(G) saved; rdy phase 3c: the initial S, then
+      // three per chunk), its (P v_new)^T has completed and the store of
+      // chunk c - 3 has read the tile buffer.
+      if (c > 0) {
+        if (!mbar_wait(rdy, c & 1, err) ||
+            !mbar_wait(&smma[(c - 1) & 1], ((c - 1) >> 1) & 1, err) ||
+            (c >= 3 && !mbar_wait(&tile_free[(c - 1) & 1], ((c - 3) >> 1) & 1, err))) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after();
+        write_output(d1_prev, (c - 1) & 1, kChunk);
+        fence_proxy_async_smem();
+        mbar_arrive(&tile_ready[(c - 1) & 1]);
+      }
+      if (!mbar_wait(&full[st], (c >> 1) & 1, err) || !wait_mma()) { ok = false; break; }
 
       // R^T = (beta V - beta exp(G) (K S))^T, hi/lo, for value column d = r64
       // and tokens [seg, seg + 16): K-major rows d (hi) and 64 + d (lo).
@@ -939,8 +890,7 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
         *reinterpret_cast<uint4*>(rimg + 8192 + sw128_chunk(r64, ch + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
       }
       ready();
-      if (!wait_issuer(false)) { ok = false; break; }  // D3 complete
-      tmem_fence_after();
+      if (!wait_mma()) { ok = false; break; }   // D3 complete
 
       // v_new for token i = r64 and value columns [seg, seg + 16): bf16 v_new
       // and v_new exp(G_C - G) as a hi/lo pair (MN-major rows i).
@@ -968,8 +918,7 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
         }
       }
       ready();
-      if (!wait_issuer(false)) { ok = false; break; }  // D5 complete
-      tmem_fence_after();
+      if (!wait_mma()) { ok = false; break; }   // D5 complete
 
       // State update (every lane): S = exp(G_C) S + K^T Vd_hi + K^T Vd_lo.
       {
@@ -989,15 +938,20 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
       prev_t0 = seq_t0 + c * kChunk;
       ready();
     }
-    // The issuer drains the tensor core, then the last output and the state.
-    if (ok) {
-      if (wait_issuer(false)) {
-        tmem_fence_after();
-        if (nchunks > 0) write_output(tmem + kTmD1 + ((nchunks - 1) & 1) * 128, (nchunks - 1) & 1, last_n);
-#pragma unroll
-        for (int j = 0; j < kDvGroup; ++j) sg[(dvh * kDvHalf + c0 + j) * kHeadDim + lrow] = s[j];
+    // The last output (after the issuer's drain commit and every thread's
+    // last state update: rdy phase 3 nchunks) and the state.
+    if (ok && wait_mma() && mbar_wait(rdy, nchunks & 1, err) &&
+        (nchunks < 3 || last_n < kChunk ||
+         mbar_wait(&tile_free[(nchunks - 1) & 1], ((nchunks - 3) >> 1) & 1, err))) {
+      if (nchunks > 0) {
+        write_output(tmem + kTmD1 + ((nchunks - 1) & 1) * 128, (nchunks - 1) & 1, last_n);
+        if (last_n == kChunk) {
+          fence_proxy_async_smem();
+          mbar_arrive(&tile_ready[(nchunks - 1) & 1]);
+        }
       }
-      ready();
+#pragma unroll
+      for (int j = 0; j < kDvGroup; ++j) sg[(dvh * kDvHalf + c0 + j) * kHeadDim + lrow] = s[j];
     }
   }
   tmem_fence_before();
