@@ -7,13 +7,14 @@
 // to 8-token recurrent slices (run_sequence, P:3387-3469).  Here every chunk
 // of every sequence is processed in two launches.
 //
-// 1. gdn_chunk_prep_kernel: chunk-parallel, one CTA per (chunk, q/k head),
-//    everything that does not depend on the recurrent state:
+// 1. gdn_chunk_prep_kernel: chunk-parallel and persistent (two CTAs per SM,
+//    units of one chunk x one q/k head, the next unit's q/k tile on its way
+//    by TMA), everything that does not depend on the recurrent state:
 //      q, k L2-norm -> the bf16 [K;Q] operand image (shared by the v-heads),
 //      [K;Q] K^T on tcgen05 (K K^T and Q K^T in one M=128 MMA),
 //      per v-head: gating g, beta, in-chunk cumsum G (warp scans),
 //      A = beta_i (K K^T)_ij exp(G_i - G_j) (strictly lower),
-//      T = (I + A)^-1 by column-parallel forward substitution in f32,
+//      T = (I + A)^-1 by 16x16 forward substitution and block merges in f32,
 //      P = (Q K^T)_ij exp(G_i - G_j) (j <= i),
 //    stored as 128-byte-swizzled operand images the second kernel feeds
 //    straight to tcgen05: T as a bf16 hi/lo pair (about 16 mantissa bits),
@@ -21,14 +22,16 @@
 // 2. gdn_chunk_state_kernel: sequential over the chunks of one sequence,
 //    one CTA per (sequence, v-head, half of the value dimension) -- column j
 //    of v_new, S and O depends only on column j of S, so the split is exact.
-//    A loader warp brings the prep records (bulk copies) and v (TMA) two
-//    chunks ahead; eight compute warps (two groups of 32 value columns) run
-//      D1 = [K;Q] S                         (K S and Q S, M=128)
-//      R  = beta V - beta exp(G) (K S)      -> bf16 hi/lo
-//      D3 = T R  (T_hi R_hi + T_lo R_hi + T_hi R_lo, M=64)   = v_new
-//      D4 = [0;P] v_new,  D5 = K^T (v_new exp(G_C - G))  (hi/lo)
-//      O  = scale (exp(G) (Q S) + P v_new),  S = exp(G_C) S + D5
-//    with the f32 state in registers (thread t owns key row t).
+//    Eight compute warps, an MMA-issuing warp and a loader warp, handing over
+//    through mbarriers; per chunk
+//      D1 = [S^T;S^T] K^T, [S^T;S^T] Q^T    ((K S)^T, (Q S)^T)
+//      R^T = (beta V - beta exp(G) (K S))^T -> bf16 hi/lo
+//      D3 = [T;T] [R_hi | R_lo] + [T_lo;T_lo] R_hi,   v_new = sum of halves
+//      D5 = K^T [Vd_hi | Vd_lo],  Vd = v_new exp(G_C - G)
+//      S = exp(G_C) S + D5
+//    and, off that chain, D4 = [Vn^T;Vn^T] P^T = (P v_new)^T and
+//    O = scale (exp(G) (Q S) + P v_new), stored by TMA, with the f32 state
+//    in registers (thread t owns key row t).
 // The reference's W = T (beta exp(G) K) is never formed:
 // v_new = U - W S = T (beta V - beta exp(G) (K S)) needs one product with T.
 // Decay factors are always exp of a non-positive difference.
