@@ -13,10 +13,12 @@
 // warp 1 issues tcgen05.mma (M=128, N=BN, K=16) from one thread with the f32
 // accumulator in TMEM (two accumulators so the epilogue of one tile overlaps
 // the main loop of the next); warps 2-5 drain TMEM with tcgen05.ld and store
-// bf16.  When there are fewer output tiles than SMs (decode rows, the 2x64
-// tail) the K dimension is split across CTAs; each split writes an f32
-// partial tile and a small pass sums the splits in a fixed order (the result
-// does not depend on scheduling) and rounds to bf16.
+// bf16.  For M <= 128 (decode rows, the 2x64 tail) the K dimension is split
+// over the CTAs of a thread-block cluster that reduce their f32 partial
+// tiles through distributed shared memory in split order; for other shapes
+// with fewer output tiles than SMs each split writes an f32 partial tile and
+// a small pass sums the splits in a fixed order.  Either way the result does
+// not depend on scheduling.
 #include <vector>
 
 #include "gdn_common.cuh"
@@ -239,6 +241,192 @@ tail_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
   }
 }
 
+// ------------------------------------------------- split-K in a cluster --
+// For M <= 128 (decode rows, the 2x64 dual tail) the K dimension is split
+// over the CTAs of one thread-block cluster (one CTA per split, up to 8).
+// Each CTA keeps its f32 partial tile in its own shared memory; after a
+// cluster barrier every CTA sums a slice of rows over the CTAs' tiles in
+// split order through distributed shared memory (deterministic) and writes
+// bf16.  No partial leaves the SMs and no second kernel runs.
+// N tile of the cluster path: 256 columns, so that the clusters of 8 of a
+// 2048-wide output (8 of them) are all resident at once.
+constexpr int kClusterBN = 256;
+
+template <int BN>
+struct ClusterGemmSmem {
+  static constexpr int kPartStride = BN + 4;   // f32 per partial-tile row (padded)
+  static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;
+  static constexpr uint32_t kBBytes = BN * kGemmBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarrierOffset = kGemmStages * kStageBytes;
+  static constexpr uint32_t kTotal = kBarrierOffset + 256 + 1024;
+  static_assert(kGemmBM * kPartStride * 4 <= kBarrierOffset, "partial tile fits the stages");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster; the CTAs of a cluster are
+// co-scheduled and reach it after bounded work only.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+tail_gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                         const __grid_constant__ CUtensorMap tmap_b, uint16_t* __restrict__ out,
+                         int M, int N, int kblocks_total, int kblocks_per_split, uint32_t* err) {
+  using L = ClusterGemmSmem<BN>;
+  constexpr int kPartStride = L::kPartStride;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
+  uint64_t* empty = full + kGemmStages;
+  uint64_t* tfull = empty + kGemmStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  float* part = reinterpret_cast<float*>(smem);   // reuses the stages once the MMAs are done
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t split = cluster_rank();
+  const uint32_t splits = cluster_size();
+  const int tn = blockIdx.x / splits;
+  const int tm = blockIdx.y;
+  const int kb0 = static_cast<int>(split) * kblocks_per_split;
+  const int kb1 = min(kb0 + kblocks_per_split, kblocks_total);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, BN);
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, err)) break;
+        mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+        uint8_t* sa = smem + stage * L::kStageBytes;
+        tma_load_2d(sa, &tmap_a, &full[stage], kb * kGemmBK, tm * kGemmBM);
+        tma_load_2d(sa + L::kABytes, &tmap_b, &full[stage], kb * kGemmBK, tn * BN);
+        if (++stage == kGemmStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kGemmBM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, err)) break;
+        tmem_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
+        const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kGemmBK / 16; ++kk)
+          umma_bf16(tmem_base, umma_sdesc(sa + kk * 32, 16, 1024), umma_sdesc(sb + kk * 32, 16, 1024),
+                    idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[stage]);
+        if (++stage == kGemmStages) { stage = 0; phase ^= 1u; }
+      }
+      umma_commit(tfull);   // also covers a split with no k-block
+    }
+    __syncwarp();
+  } else {
+    // Warps 2..5: TMEM lanes 32*(w%4) .. +31 -> rows of the partial tile.
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const bool done = mbar_wait(tfull, 0, err);
+    tmem_fence_after();
+    float* prow = part + row * kPartStride;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      tmem_ld16(tmem_addr(tmem_base, quarter * 32, c), r);
+      tmem_ld_wait();
+      const bool live = done && kb1 > kb0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        reinterpret_cast<float4*>(prow + c)[j] =
+            live ? make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]))
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  cluster_sync_all();   // every partial tile written
+
+  // Rows [split * 128 / splits, +128 / splits) of the tile: sum the splits'
+  // partials in split order, round to bf16.
+  {
+    const int rows_per = kGemmBM / static_cast<int>(splits);
+    const int r0 = static_cast<int>(split) * rows_per;
+    const uint32_t pbase = smem_u32(part);
+    for (int idx = threadIdx.x; idx < rows_per * (BN / 4); idx += kGemmThreads) {
+      const int rr = r0 + idx / (BN / 4);
+      const int c4 = idx % (BN / 4);
+      const uint32_t a = pbase + static_cast<uint32_t>((rr * kPartStride + c4 * 4) * 4);
+      // All remote loads in flight at once, then the sum in split order.
+      float4 v[8];
+#pragma unroll
+      for (uint32_t s = 0; s < 8; ++s)
+        v[s] = (s < splits) ? ld_cluster_f4(a, s) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 acc = v[0];
+#pragma unroll
+      for (uint32_t s = 1; s < 8; ++s) {
+        if (s < splits) { acc.x += v[s].x; acc.y += v[s].y; acc.z += v[s].z; acc.w += v[s].w; }
+      }
+      const int grow = tm * kGemmBM + rr;
+      if (grow < M) {
+        uint2 w;
+        w.x = pack_bf16x2(acc.x, acc.y);
+        w.y = pack_bf16x2(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(out + static_cast<int64_t>(grow) * N + tn * BN + c4 * 4) = w;
+      }
+    }
+  }
+  cluster_sync_all();   // no CTA leaves while another still reads its tile
+
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tmem_fence_after();
+    tmem_dealloc(tmem_base, BN);
+  }
+}
+
 // out = bf16(sum over splits of ws[split]) in split order.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, uint16_t* __restrict__ out,
                                      int64_t n4, int splits) {
@@ -294,6 +482,7 @@ static bool make_tmap_bf16(CUtensorMap* map, const void* base, int64_t rows, int
 
 struct TailGemmPlan {
   int bn, tiles_m, tiles_n, splits, kblocks_total, kblocks_per_split, grid;
+  bool cluster;   // split-K reduced inside a thread-block cluster (M <= 128)
 };
 
 static int sm_count() {
@@ -310,6 +499,23 @@ static int sm_count() {
 
 TailGemmPlan plan_tail_gemm(int64_t M, int N, int K) {
   TailGemmPlan p{};
+  if (M <= kGemmBM && N % kClusterBN == 0) {
+    // One row tile: N tiles of 128 columns, K split over a cluster of up to
+    // 8 CTAs (the largest power of two that divides the k-blocks).
+    p.cluster = true;
+    p.bn = kClusterBN;
+    p.tiles_m = 1;
+    p.tiles_n = N / kClusterBN;
+    p.kblocks_total = K / kGemmBK;
+    p.splits = 1;
+    for (int sp = 8; sp >= 2; sp >>= 1) {
+      if (p.kblocks_total % sp == 0) { p.splits = sp; break; }
+    }
+    p.kblocks_per_split = p.kblocks_total / p.splits;
+    p.grid = p.tiles_n * p.splits;
+    return p;
+  }
+  p.cluster = false;
   p.bn = (N % 256 == 0) ? 256 : 128;
   p.tiles_m = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
   p.tiles_n = N / p.bn;
@@ -333,7 +539,7 @@ TailGemmPlan plan_tail_gemm(int64_t M, int N, int K) {
 
 uint64_t tail_gemm_workspace_bytes(int64_t M, int N, int K) {
   const TailGemmPlan p = plan_tail_gemm(M, N, K);
-  return p.splits > 1 ? static_cast<uint64_t>(p.splits) * M * N * sizeof(float) : 0;
+  return (p.splits > 1 && !p.cluster) ? static_cast<uint64_t>(p.splits) * M * N * sizeof(float) : 0;
 }
 
 cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uint16_t* gamma,
@@ -370,6 +576,26 @@ cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out
   CUtensorMap ta, tb;
   if (!make_tmap_bf16(&ta, a, M, K, kGemmBM) || !make_tmap_bf16(&tb, w, N, K, p.bn))
     return cudaErrorInvalidValue;
+  if (p.cluster) {
+    const uint32_t smem = ClusterGemmSmem<kClusterBN>::kTotal;
+    cudaError_t ec = cudaFuncSetAttribute(tail_gemm_cluster_kernel<kClusterBN>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (ec != cudaSuccess) return ec;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(p.splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tail_gemm_cluster_kernel<kClusterBN>, ta, tb, out, static_cast<int>(M), N,
+                              p.kblocks_total, p.kblocks_per_split, err);
+  }
   cudaError_t e = (p.bn == 256) ? launch_gemm_bn<256>(ta, tb, out, ws, M, N, p, err, stream)
                                 : launch_gemm_bn<128>(ta, tb, out, ws, M, N, p, err, stream);
   if (e != cudaSuccess) return e;
