@@ -41,11 +41,15 @@ def test_output_tail_rejects(kwargs, fragment):
 
 
 def test_output_tail_workspace_size():
-    # error word + gated activations (+ split-K partials when K is split)
+    # error word + gated activations (+ f32 split-K partials when K is split
+    # across separate CTAs; up to 128 rows the split is reduced inside a
+    # thread-block cluster and needs no partials)
     n = G.output_tail_workspace_bytes(8192, 32, 2048)
     assert n == 256 + 8192 * 4096 * 2
     small = G.output_tail_workspace_bytes(128, 32, 2048)
-    assert small > 256 + 128 * 4096 * 2
+    assert small == 256 + 128 * 4096 * 2
+    mid = G.output_tail_workspace_bytes(512, 32, 2048)
+    assert mid > 256 + 512 * 4096 * 2
 
 
 def _cu(values):
