@@ -51,7 +51,8 @@ def oracle_core(x, cu):
 
 @pytest.mark.parametrize("rows,hv,hidden", [(128, 32, 2048), (1, 32, 2048), (64, 32, 2048),
                                             (130, 32, 2048), (1000, 32, 2048),
-                                            (256, 4, 2048), (96, 8, 384)])
+                                            (256, 4, 2048), (96, 8, 384),
+                                            (64, 4, 2048), (32, 2, 2048)])
 def test_output_tail_matches_oracle(cuda, rows, hv, hidden):
     import torch
     D = G.HEAD_DIM
