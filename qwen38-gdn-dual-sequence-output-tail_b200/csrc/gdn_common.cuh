@@ -151,7 +151,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled bulk tensor load into this CTA's shared memory (no multicast).
+// 2-D tiled bulk tensor load into this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int32_t c0, int32_t c1) {
   asm volatile(
@@ -161,7 +161,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// 3-D tiled bulk tensor load into this CTA's shared memory (no multicast).
+// 3-D tiled bulk tensor load into this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int32_t c0, int32_t c1, int32_t c2) {
   asm volatile(
@@ -208,7 +208,7 @@ __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
-// 1-D bulk copy global -> this CTA's shared memory (no multicast).  Both
+// 1-D bulk copy global -> this CTA's own shared memory.  Both
 // addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
                                           uint64_t* bar) {
