@@ -9,9 +9,12 @@ One process per GPU (torchrun for N > 1).  With N GPUs the heads are split
 evenly across ranks (head-parallel; rank r holds v-heads [r*32/N, (r+1)*32/N)
 and the matching q/k heads and out_proj columns) and every rank processes 2*N
 sequences of 4096 tokens, so the per-rank kernel work is that of one GPU
-("weak" scaling); the rank-partial [tokens, 2048] outputs are summed with a
-bf16 NCCL all-reduce inside the timed region.  One JSON line is printed by
-rank 0.
+("weak" scaling); the rank-partial [tokens, 2048] outputs are summed inside
+the timed region, by default inside the tail GEMM kernel itself over NVLink
+peer memory (``--reduce fused``; ``--reduce nccl`` runs the unfused tail and a
+bf16 NCCL all-reduce instead).  The end-to-end figure goes through the
+provider ABI, whose output is the rank-partial as in the reference, followed
+by an NCCL all-reduce.  One JSON line is printed by rank 0.
 
 ``--impl reference`` times the CPU restatement of the reference path (the
 oracle; the reference itself runs only on Ascend NPUs) on the host cores with
@@ -171,6 +174,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--reduce", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: rank sum fused into the tail GEMM over NVLink peer memory "
+                         "(default), or a separate NCCL all-reduce")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -216,7 +222,30 @@ def main():
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)
 
+    fused = world > 1 and args.reduce == "fused"
+    group = None
+    if fused:
+        # Every rank's exchange region mapped into every rank (CUDA IPC
+        # handles passed through the process group).
+        def exchange(payload):
+            got = [None] * world
+            dist.all_gather_object(got, payload)
+            return got
+
+        group = G.TailGroup(T, HIDDEN, rank, world, dev, exchange=exchange)
+        o_buf = torch.empty_like(t["v"])
+        ws_chunk = torch.empty(G.chunk_prefill_workspace_bytes(cu, hk, hv), dtype=torch.uint8,
+                               device=dev)
+        ws_ar = torch.empty(G.output_tail_allreduce_workspace_bytes(T, hv), dtype=torch.uint8,
+                            device=dev)
+
     def step():
+        if fused:
+            G.chunk_prefill(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"], t["dt_bias"],
+                            t["state"], cu, o_out=o_buf, workspace=ws_chunk, stream=stream)
+            group.output_tail(o_buf, t["z"], t["gamma"], t["w_out"], workspace=ws_ar,
+                              stream=stream)
+            return
         G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
                         t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu, out=out,
                         workspace=ws, stream=stream)
@@ -247,11 +276,11 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    G.workspace_status(ws)
+    G.workspace_status(ws_ar if fused else ws, stream)
     with ClockSampler(local) as clocks:
         ms = timed(step, args.steps, 0)
     clk = clocks.summary()
-    G.workspace_status(ws)
+    G.workspace_status(ws_ar if fused else ws, stream)
     tokens_total = T  # every rank sees all tokens of its shard; tokens are not duplicated
     value = tokens_total / (ms * 1e-3)
 
@@ -265,8 +294,14 @@ def main():
     core_ms = timed(lambda: G.chunk_prefill(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"],
                                             t["dt_bias"], t["state"], cu, o_out=o,
                                             workspace=ws_core, stream=stream), args.steps, 2)
-    tail_ms = timed(lambda: G.output_tail(o, t["z"], t["gamma"], t["w_out"], out=out,
-                                          workspace=ws_tail, stream=stream), args.steps, 2)
+    if fused:
+        # the tail with the rank sum fused in (what the step runs)
+        tail_ms = timed(lambda: group.output_tail(o, t["z"], t["gamma"], t["w_out"],
+                                                  workspace=ws_ar, stream=stream), args.steps, 2)
+        G.workspace_status(ws_ar, stream)
+    else:
+        tail_ms = timed(lambda: G.output_tail(o, t["z"], t["gamma"], t["w_out"], out=out,
+                                              workspace=ws_tail, stream=stream), args.steps, 2)
     hbm_peak, tf_peak, peak_kind = load_peaks()
     chunks = nseq * (SEQ_LEN // 64)
     core_flop = CHUNK_MFLOP * 1e6 * chunks * hv
@@ -339,7 +374,10 @@ def main():
             "data": "synthetic (seeded SplitMix64/Box-Muller, benchmark distributions)",
             "config": {"workload": workload, "tokens_per_step": T,
                        "sequences": nseq, "seq_len": SEQ_LEN,
-                       "parallelism": f"head-parallel tp{world}" + (" + nccl all-reduce" if world > 1 else ""),
+                       "parallelism": f"head-parallel tp{world}" + (
+                           "" if world == 1 else
+                           " + rank sum fused into the tail GEMM (NVLink peer memory)" if fused
+                           else " + nccl all-reduce"),
                        "l2": "inputs larger than L2 (q,k,v,z = %.0f MB per step)" %
                              (sum(v.numel() * v.element_size() for n, v in t.items()
                                   if n in ("q", "k", "v", "z")) / 1e6)},
@@ -353,7 +391,10 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
+        if group is not None:
+            group.close()
         dist.destroy_process_group()
 
 

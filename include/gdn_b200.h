@@ -141,6 +141,65 @@ GDN_B200_API int32_t gdn_b200_layer_forward(const void* q, const void* k, const 
                                int32_t hidden, void* workspace,
                                uint64_t workspace_bytes, void* stream);
 
+/* ----------------------------------------------------------------------
+ * Head-parallel output tail with the rank reduction fused in.
+ *
+ * With the value heads split over world_size GPUs of one node (rank r holds
+ * value_heads = Hv / world_size heads, the matching o and z columns and the
+ * w_out columns [r * value_heads * 128, (r + 1) * value_heads * 128)), each
+ * rank's tail yields a partial [rows, hidden].  The reference returns that
+ * rank-partial (P:3541-3547) and leaves the sum to its engine; this entry
+ * point (no counterpart in the reference) sums it inside the tail GEMM
+ * kernel over NVLink peer memory, tile by tile, and leaves the full output
+ * on every rank:
+ *   out = bf16( f32(owning rank's partial) + sum over the other ranks, in
+ *               rank order, of bf16(their partial) ),
+ * the same bits on every rank.
+ *
+ * Each rank owns an exchange region of gdn_b200_tail_exchange_bytes bytes
+ * (gdn_b200_exchange_alloc: zero-filled device memory of the current
+ * device).  It holds the rank's output at offset 0 ([max_rows, hidden] bf16;
+ * the first rows * hidden elements are valid after a call) and the staging
+ * space and flags of the exchange.  Ranks map one another's regions with
+ * gdn_b200_exchange_export / gdn_b200_exchange_open (CUDA IPC: the handle is
+ * GDN_B200_EXCHANGE_HANDLE_BYTES plain bytes, passed between the processes by
+ * any means) and list them, by rank, in a gdn_b200_tail_group_v1.
+ *
+ * Every rank calls gdn_b200_output_tail_allreduce with the same rows, hidden,
+ * max_rows and epoch; epochs start at 1 and grow by one per call.  The
+ * kernels of the ranks wait for one another, bounded: if a rank does not take
+ * part, the others end with a device error (gdn_b200_workspace_status) after
+ * 2 s.  After a failed call the regions must be freed and allocated again.
+ */
+#define GDN_B200_MAX_RANKS 8
+#define GDN_B200_EXCHANGE_HANDLE_BYTES 64
+
+typedef struct gdn_b200_tail_group_v1 {
+  int32_t rank;
+  int32_t world_size;                /* 1, 2, 4 or 8 */
+  int64_t max_rows;                  /* rows the regions were sized for */
+  int32_t hidden;                    /* a multiple of 256 */
+  int32_t reserved;                  /* must be 0 */
+  void* region[GDN_B200_MAX_RANKS];  /* rank i's exchange region as mapped here */
+} gdn_b200_tail_group_v1;
+
+GDN_B200_API uint64_t gdn_b200_tail_exchange_bytes(int64_t max_rows, int32_t hidden,
+                                                   int32_t world_size);
+GDN_B200_API int32_t gdn_b200_exchange_alloc(uint64_t bytes, void** region);
+GDN_B200_API int32_t gdn_b200_exchange_free(void* region);
+GDN_B200_API int32_t gdn_b200_exchange_export(const void* region, void* handle);
+GDN_B200_API int32_t gdn_b200_exchange_open(const void* handle, void** region);
+GDN_B200_API int32_t gdn_b200_exchange_close(void* region);
+GDN_B200_API uint64_t gdn_b200_output_tail_allreduce_workspace_bytes(int64_t rows,
+                                                                     int32_t value_heads);
+GDN_B200_API int32_t gdn_b200_output_tail_allreduce(const void* o, const void* z,
+                                                    const void* gamma, const void* w_out,
+                                                    int64_t rows, int32_t value_heads,
+                                                    int32_t hidden, float eps,
+                                                    const gdn_b200_tail_group_v1* group,
+                                                    uint32_t epoch, void* workspace,
+                                                    uint64_t workspace_bytes, void* stream);
+
 /* Seeded synthetic inputs (host side, used by benchmarks and tests).
  * Element i of tensor `tensor_id` under `seed` is a pure function of
  * (seed, tensor_id, i): SplitMix64 counters, Box-Muller for normals.

@@ -127,6 +127,135 @@ int32_t gdn_b200_output_tail(const void* o, const void* z, const void* gamma, co
   return cuda_status(e, "tail GEMM launch");
 }
 
+// ------------------------------------------- head-parallel fused tail ----
+
+static_assert(GDN_B200_MAX_RANKS == gdn::kTailMaxRanks, "rank limit");
+static_assert(GDN_B200_EXCHANGE_HANDLE_BYTES == sizeof(cudaIpcMemHandle_t), "IPC handle size");
+
+uint64_t gdn_b200_tail_exchange_bytes(int64_t max_rows, int32_t hidden, int32_t world_size) {
+  gdn::TailExchangeLayout L;
+  if (!gdn::tail_exchange_layout(max_rows, hidden, world_size, &L)) return 0;
+  return L.total;
+}
+
+int32_t gdn_b200_exchange_alloc(uint64_t bytes, void** region) {
+  if (region == nullptr) return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "region is null");
+  *region = nullptr;
+  if (bytes == 0) return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "bytes must be positive");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMalloc(exchange region)");
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_status(e, "cudaMemset(exchange region)");
+  }
+  *region = p;
+  return ok();
+}
+
+int32_t gdn_b200_exchange_free(void* region) {
+  if (region == nullptr) return ok();
+  return cuda_status(cudaFree(region), "cudaFree(exchange region)");
+}
+
+int32_t gdn_b200_exchange_export(const void* region, void* handle) {
+  if (region == nullptr || handle == nullptr)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(region));
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  return ok();
+}
+
+int32_t gdn_b200_exchange_open(const void* handle, void** region) {
+  if (handle == nullptr || region == nullptr)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
+  *region = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcOpenMemHandle");
+  *region = p;
+  return ok();
+}
+
+int32_t gdn_b200_exchange_close(void* region) {
+  if (region == nullptr) return ok();
+  return cuda_status(cudaIpcCloseMemHandle(region), "cudaIpcCloseMemHandle");
+}
+
+uint64_t gdn_b200_output_tail_allreduce_workspace_bytes(int64_t rows, int32_t value_heads) {
+  if (rows < 0 || value_heads <= 0) return 0;
+  return kErrBytes + round256(static_cast<uint64_t>(rows) * value_heads * GDN_B200_HEAD_DIM * 2);
+}
+
+int32_t gdn_b200_output_tail_allreduce(const void* o, const void* z, const void* gamma,
+                                       const void* w_out, int64_t rows, int32_t value_heads,
+                                       int32_t hidden, float eps,
+                                       const gdn_b200_tail_group_v1* group, uint32_t epoch,
+                                       void* workspace, uint64_t workspace_bytes,
+                                       void* stream) {
+  if (rows < 0 || value_heads <= 0 || hidden <= 0)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "rows, value_heads and hidden must be positive");
+  if (hidden % 256 != 0)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "hidden must be a multiple of 256");
+  if (rows > (int64_t{1} << 31) / 2)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "too many rows");
+  if (!(eps > 0.0f) || !std::isfinite(eps))
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "eps must be positive");
+  if (o == nullptr || z == nullptr || gamma == nullptr || w_out == nullptr ||
+      workspace == nullptr || group == nullptr)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
+  if (!aligned16(o) || !aligned16(z) || !aligned16(w_out) || !aligned16(workspace) ||
+      !aligned16(gamma))
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  const int world = group->world_size;
+  if (world != 1 && world != 2 && world != 4 && world != 8)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "group world_size must be 1, 2, 4 or 8");
+  if (group->rank < 0 || group->rank >= world)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "group rank out of range");
+  if (group->reserved != 0)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "group reserved field must be 0");
+  if (group->hidden != hidden)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "hidden differs from the group's");
+  if (rows > group->max_rows)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "rows exceed the group's max_rows");
+  gdn::TailExchangeLayout layout;
+  if (!gdn::tail_exchange_layout(group->max_rows, hidden, world, &layout))
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "invalid group geometry");
+  gdn::TailPeerRegions peers{};
+  for (int i = 0; i < world; ++i) {
+    if (group->region[i] == nullptr)
+      return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "group region is null");
+    if ((reinterpret_cast<uintptr_t>(group->region[i]) & 255u) != 0)
+      return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "group regions must be 256-byte aligned");
+    peers.region[i] = static_cast<uint8_t*>(group->region[i]);
+  }
+  if (epoch == 0) return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "epoch must start at 1");
+  const uint64_t need = gdn_b200_output_tail_allreduce_workspace_bytes(rows, value_heads);
+  if (workspace_bytes < need)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT,
+                "workspace too small: need " + std::to_string(need) + " bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws);
+  uint16_t* gated = reinterpret_cast<uint16_t*>(ws + kErrBytes);
+  const int K = value_heads * GDN_B200_HEAD_DIM;
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync");
+  if (rows == 0) return ok();
+  e = gdn::launch_tail_prologue(static_cast<const uint16_t*>(o), static_cast<const uint16_t*>(z),
+                                static_cast<const uint16_t*>(gamma), gated, rows, value_heads,
+                                eps, s);
+  if (e != cudaSuccess) return cuda_status(e, "tail prologue launch");
+  e = gdn::launch_tail_gemm_allreduce(gated, static_cast<const uint16_t*>(w_out), rows, hidden, K,
+                                      peers, group->rank, world, layout, epoch, err, s);
+  return cuda_status(e, "fused tail launch");
+}
+
 // ----------------------------------------------------------- decode ----
 
 int32_t gdn_b200_decode_step(const void* q, const void* k, const void* v, const void* a,

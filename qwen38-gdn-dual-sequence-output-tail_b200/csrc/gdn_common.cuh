@@ -41,6 +41,52 @@ __device__ __forceinline__ void record_error(uint32_t* err, uint32_t code) {
   if (err != nullptr) atomicCAS(err, 0u, code);
 }
 
+// ------------------------------------------------- cross-GPU signalling --
+// Flags that live in one GPU's memory and are written by another GPU over an
+// NVLink mapping.  A writer makes its earlier stores visible with a
+// system-scope release; a reader acquires the flag before it reads the data.
+// Flags carry a call epoch that only grows, so they are never reset.
+
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Orders this thread's earlier generic-proxy accesses of global memory
+// before its later TMA (async-proxy) reads.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Waits until the flag has reached `epoch` (wrap-safe comparison), bounded
+// by the same wall-clock limit as every other wait; on expiry records
+// kErrWaitTimeout and returns false.
+__device__ __forceinline__ bool wait_flag_reached(const uint32_t* flag, uint32_t epoch,
+                                                  uint32_t* err) {
+  if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const unsigned long long start = global_ns();
+  for (uint32_t poll = 1;; ++poll) {
+    if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+    if ((poll & 15u) == 0u) {
+      if (global_ns() - start > kWaitLimitNs) {
+        record_error(err, kErrWaitTimeout);
+        return false;
+      }
+      if (err != nullptr && *reinterpret_cast<volatile uint32_t*>(err) != 0) return false;
+    }
+    __nanosleep(40);
+  }
+}
+
 // ------------------------------------------------------------- bf16 -----
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {

@@ -36,4 +36,27 @@ cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uin
 cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out, float* ws,
                              int64_t M, int N, int K, uint32_t* err, cudaStream_t stream);
 
+// Head-parallel tail with the rank reduction fused in (gdn_tail_allreduce.cu).
+constexpr int kTailMaxRanks = 8;
+constexpr int kTailArGrid = 148;  // CTAs per rank (same on every rank)
+
+// Every rank's exchange region as mapped in this process.
+struct TailPeerRegions {
+  uint8_t* region[kTailMaxRanks];
+};
+
+// Exchange region of one rank, sized for up to max_rows rows: the rank's
+// output [max_rows, hidden] bf16 at offset 0, then the staging area for the
+// partial tiles other ranks send it ([slots * world * 128, 256] bf16), the
+// per-(tile, source rank, warp) flags and the per-(CTA, source rank) done
+// flags (u32, zero at allocation).
+struct TailExchangeLayout {
+  uint64_t out_bytes, staging_off, staging_rows, flags_off, done_off, total;
+};
+bool tail_exchange_layout(int64_t max_rows, int hidden, int world, TailExchangeLayout* out);
+cudaError_t launch_tail_gemm_allreduce(const uint16_t* a, const uint16_t* w, int64_t M, int N,
+                                       int K, const TailPeerRegions& peers, int rank, int world,
+                                       const TailExchangeLayout& layout, uint32_t epoch,
+                                       uint32_t* err, cudaStream_t stream);
+
 }  // namespace gdn

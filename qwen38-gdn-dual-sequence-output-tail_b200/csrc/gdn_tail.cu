@@ -21,8 +21,8 @@
 // not depend on scheduling.
 #include <vector>
 
-#include "gdn_common.cuh"
 #include "gdn_internal.h"
+#include "gdn_tail_gemm.cuh"
 
 namespace gdn {
 
@@ -73,20 +73,6 @@ tail_prologue_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict_
 }
 
 // ---------------------------------------------------------------- GEMM --
-
-constexpr int kGemmBM = 128;
-constexpr int kGemmBK = 64;
-constexpr int kGemmStages = 4;
-constexpr int kGemmThreads = 192;
-
-template <int BN>
-struct GemmSmem {
-  static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;
-  static constexpr uint32_t kBBytes = BN * kGemmBK * 2;
-  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kBarrierOffset = kGemmStages * kStageBytes;
-  static constexpr uint32_t kTotal = kBarrierOffset + 256 + 1024;  // + alignment slack
-};
 
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -464,9 +450,7 @@ static EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-// Row-major bf16 matrix [rows, cols] (cols contiguous), box [box_rows, 64]
-// with 128-byte swizzle; rows beyond the matrix read as zero.
-static bool make_tmap_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
+bool make_tmap_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
                            int box_rows) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (fn == nullptr) return false;
@@ -485,7 +469,7 @@ struct TailGemmPlan {
   bool cluster;   // split-K reduced inside a thread-block cluster (M <= 128)
 };
 
-static int sm_count() {
+int sm_count() {
   static int count = 0;
   if (count == 0) {
     int dev = 0;

@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import struct
 from dataclasses import dataclass
 
 import numpy as np
@@ -45,6 +46,14 @@ EXPORTED_SYMBOLS = (
     "gdn_b200_layer_forward_workspace_bytes",
     "gdn_b200_layer_forward",
     "gdn_b200_fill_synthetic",
+    "gdn_b200_tail_exchange_bytes",
+    "gdn_b200_exchange_alloc",
+    "gdn_b200_exchange_free",
+    "gdn_b200_exchange_export",
+    "gdn_b200_exchange_open",
+    "gdn_b200_exchange_close",
+    "gdn_b200_output_tail_allreduce_workspace_bytes",
+    "gdn_b200_output_tail_allreduce",
     "statecentric_qwen38_provider_query_v1",
 )
 
@@ -88,6 +97,24 @@ def lib() -> ctypes.CDLL:
         L.gdn_b200_layer_forward.restype = i32
         L.gdn_b200_fill_synthetic.argtypes = [u64, u64, u64, i32, f32, f32, i32, vp]
         L.gdn_b200_fill_synthetic.restype = i32
+        L.gdn_b200_tail_exchange_bytes.argtypes = [i64, i32, i32]
+        L.gdn_b200_tail_exchange_bytes.restype = u64
+        L.gdn_b200_exchange_alloc.argtypes = [u64, ctypes.POINTER(vp)]
+        L.gdn_b200_exchange_alloc.restype = i32
+        L.gdn_b200_exchange_free.argtypes = [vp]
+        L.gdn_b200_exchange_free.restype = i32
+        L.gdn_b200_exchange_export.argtypes = [vp, vp]
+        L.gdn_b200_exchange_export.restype = i32
+        L.gdn_b200_exchange_open.argtypes = [vp, ctypes.POINTER(vp)]
+        L.gdn_b200_exchange_open.restype = i32
+        L.gdn_b200_exchange_close.argtypes = [vp]
+        L.gdn_b200_exchange_close.restype = i32
+        L.gdn_b200_output_tail_allreduce_workspace_bytes.argtypes = [i64, i32]
+        L.gdn_b200_output_tail_allreduce_workspace_bytes.restype = u64
+        L.gdn_b200_output_tail_allreduce.argtypes = [vp, vp, vp, vp, i64, i32, i32, f32,
+                                                     ctypes.POINTER(TailGroupV1), ctypes.c_uint32,
+                                                     vp, u64, vp]
+        L.gdn_b200_output_tail_allreduce.restype = i32
         _lib = L
     return _lib
 
@@ -197,6 +224,117 @@ def layer_forward(q, k, v, a, b, z, A_log, dt_bias, gamma, w_out, state, cu_seql
                                         _ptr(state), _ptr(out), p, len(arr) - 1, hk, hv, hidden,
                                         _ptr(workspace), workspace.numel(), _stream(stream)))
     return out
+
+
+# ------------------------------------------------- head-parallel tail --
+
+MAX_RANKS = 8
+EXCHANGE_HANDLE_BYTES = 64
+
+
+class TailGroupV1(ctypes.Structure):
+    """gdn_b200_tail_group_v1 of include/gdn_b200.h."""
+    _fields_ = [("rank", ctypes.c_int32), ("world_size", ctypes.c_int32),
+                ("max_rows", ctypes.c_int64), ("hidden", ctypes.c_int32),
+                ("reserved", ctypes.c_int32), ("region", ctypes.c_void_p * MAX_RANKS)]
+
+
+class _DeviceArray:
+    """A raw device allocation presented to torch through
+    ``__cuda_array_interface__`` (the tensor keeps this object alive)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(int(d) for d in shape),
+                                         "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3}
+
+
+def tail_exchange_bytes(max_rows: int, hidden: int, world_size: int) -> int:
+    return int(lib().gdn_b200_tail_exchange_bytes(max_rows, hidden, world_size))
+
+
+def output_tail_allreduce_workspace_bytes(rows: int, value_heads: int) -> int:
+    return int(lib().gdn_b200_output_tail_allreduce_workspace_bytes(rows, value_heads))
+
+
+class TailGroup:
+    """One rank of a head-parallel output-tail group
+    (``gdn_b200_output_tail_allreduce``): the rank's exchange region, the
+    other ranks' regions mapped into this process, and the call epoch.
+
+    ``exchange(payload: bytes) -> list[bytes]`` returns every rank's payload
+    in rank order (for example around ``torch.distributed.all_gather_object``);
+    it is called once, here, when ``world_size > 1``.  ``out`` is this rank's
+    output ``[max_rows, hidden]`` bf16 inside its region.  Every rank must
+    call :meth:`output_tail` the same number of times with the same rows, and
+    :meth:`close` only after every rank's last call has finished (a barrier).
+    """
+
+    def __init__(self, max_rows: int, hidden: int, rank: int, world_size: int, device,
+                 exchange=None):
+        import torch
+        self.device = torch.device(device)
+        self.max_rows, self.hidden = int(max_rows), int(hidden)
+        self.rank, self.world_size = int(rank), int(world_size)
+        nbytes = tail_exchange_bytes(max_rows, hidden, world_size)
+        if nbytes == 0:
+            raise GdnError(INVALID_ARGUMENT, "invalid tail group geometry")
+        self._opened = []
+        region = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _check(lib().gdn_b200_exchange_alloc(nbytes, ctypes.byref(region)))
+        self._own = region.value
+        regions = [None] * world_size
+        regions[rank] = self._own
+        if world_size > 1:
+            handle = (ctypes.c_uint8 * EXCHANGE_HANDLE_BYTES)()
+            _check(lib().gdn_b200_exchange_export(ctypes.c_void_p(self._own), handle))
+            # The geometry travels with the handle: regions laid out for
+            # different sizes would put a peer's flags outside this region.
+            geometry = struct.pack("<qii", max_rows, hidden, world_size)
+            payloads = exchange(bytes(handle) + geometry)
+            if len(payloads) != world_size:
+                raise GdnError(INVALID_ARGUMENT, "exchange returned the wrong number of handles")
+            if any(bytes(pl[EXCHANGE_HANDLE_BYTES:]) != geometry for pl in payloads):
+                self.close()
+                raise GdnError(INVALID_ARGUMENT, "ranks disagree on max_rows, hidden or world size")
+            for i, payload in enumerate(payloads):
+                if i == rank:
+                    continue
+                h = (ctypes.c_uint8 * EXCHANGE_HANDLE_BYTES).from_buffer_copy(
+                    bytes(payload[:EXCHANGE_HANDLE_BYTES]))
+                peer = ctypes.c_void_p()
+                with torch.cuda.device(self.device):
+                    _check(lib().gdn_b200_exchange_open(h, ctypes.byref(peer)))
+                regions[i] = peer.value
+                self._opened.append(peer.value)
+        self.group = TailGroupV1(rank, world_size, max_rows, hidden, 0,
+                                 (ctypes.c_void_p * MAX_RANKS)(*regions))
+        self.out = torch.as_tensor(_DeviceArray(self._own, (max_rows, hidden), "<i2"),
+                                   device=self.device).view(torch.bfloat16)
+        self.epoch = 0
+
+    def output_tail(self, o, z, gamma, w_out, eps=1e-6, workspace=None, stream=None):
+        """Fused tail of this rank's heads plus the rank sum; returns the
+        first ``rows`` rows of :attr:`out` (the same values on every rank)."""
+        rows, hv = o.shape[0], o.shape[1]
+        if workspace is None:
+            workspace = _workspace(output_tail_allreduce_workspace_bytes(rows, hv), o.device)
+        self.epoch += 1
+        _check(lib().gdn_b200_output_tail_allreduce(
+            _ptr(o), _ptr(z), _ptr(gamma), _ptr(w_out), rows, hv, self.hidden, eps,
+            ctypes.byref(self.group), self.epoch, _ptr(workspace), workspace.numel(),
+            _stream(stream)))
+        return self.out[:rows]
+
+    def close(self) -> None:
+        for p in self._opened:
+            lib().gdn_b200_exchange_close(ctypes.c_void_p(p))
+        self._opened = []
+        if self._own is not None:
+            self.out = None
+            lib().gdn_b200_exchange_free(ctypes.c_void_p(self._own))
+            self._own = None
 
 
 def workspace_status(workspace, stream=None) -> None:

@@ -1,8 +1,9 @@
-/* Prints sizeof/offsetof of the provider ABI structures so the test can
+/* Prints sizeof/offsetof of the provider ABI structures and the tail group so the test can
  * compare them with the ctypes mirror used by the Python bindings. */
 #include <stddef.h>
 #include <stdio.h>
 
+#include "gdn_b200.h"
 #include "statecentric_qwen38_provider_api_v1.h"
 
 #define F(T, m) printf("%s.%s %zu\n", #T, #m, offsetof(T, m))
@@ -27,6 +28,8 @@ int main(void) {
   F(statecentric_qwen38_provider_descriptor_v1, create);
   F(statecentric_qwen38_provider_descriptor_v1, release_error);
   F(statecentric_qwen38_provider_descriptor_v1, reserved2);
+  S(gdn_b200_tail_group_v1); F(gdn_b200_tail_group_v1, max_rows);
+  F(gdn_b200_tail_group_v1, hidden); F(gdn_b200_tail_group_v1, region);
   printf("MIN_SIZE %zu\n", (size_t)STATECENTRIC_QWEN38_PROVIDER_DESCRIPTOR_V1_MIN_SIZE);
   return 0;
 }

@@ -204,3 +204,77 @@ def test_cancel_is_unsupported():
     assert d.cancel(None, None, ctypes.byref(err)) == G.UNSUPPORTED
     assert b"cannot be cancelled" in err.contents.message
     d.release_error(err)
+
+
+# ------------------------------------------------- head-parallel fused tail --
+
+def _group(rank=0, world=2, max_rows=256, hidden=2048, reserved=0, regions=None):
+    if regions is None:
+        regions = [0x100000 * (i + 1) for i in range(world)]
+    arr = (ctypes.c_void_p * G.MAX_RANKS)(*(regions + [None] * (G.MAX_RANKS - len(regions))))
+    return G.TailGroupV1(rank, world, max_rows, hidden, reserved, arr)
+
+
+def tail_ar(group, rows=128, hv=16, hidden=2048, eps=1e-6, epoch=1, ws=FAKE, ws_bytes=1 << 40,
+            o=FAKE):
+    return lib().gdn_b200_output_tail_allreduce(o, FAKE, FAKE, FAKE, rows, hv, hidden, eps,
+                                                ctypes.byref(group) if group is not None else None,
+                                                epoch, ws, ws_bytes, None)
+
+
+@pytest.mark.parametrize("gkw,ckw,fragment", [
+    ({}, dict(hidden=2176), "multiple of 256"),
+    ({}, dict(rows=-1), "positive"),
+    (dict(world=3, regions=[0x100000, 0x200000, 0x300000]), {}, "world_size"),
+    (dict(rank=2), {}, "rank"),
+    (dict(reserved=1), {}, "reserved"),
+    (dict(hidden=1024), {}, "hidden differs"),
+    ({}, dict(rows=257), "max_rows"),
+    (dict(regions=[0x100000, None]), {}, "region is null"),
+    (dict(regions=[0x100000, 0x100010]), {}, "256-byte aligned"),
+    ({}, dict(epoch=0), "epoch"),
+    ({}, dict(ws_bytes=100), "workspace too small"),
+    ({}, dict(o=ODD), "aligned"),
+])
+def test_output_tail_allreduce_rejects(gkw, ckw, fragment):
+    assert tail_ar(_group(**gkw), **ckw) == G.INVALID_ARGUMENT
+    assert fragment in G.last_error()
+
+
+def test_output_tail_allreduce_rejects_null_group():
+    assert tail_ar(None) == G.INVALID_ARGUMENT
+    assert "null" in G.last_error()
+
+
+def test_tail_exchange_layout_sizes():
+    # [max_rows, hidden] bf16 output, then per owned tile slot one 64 KB
+    # staging tile per rank, per-(tile, rank, warp) flags, per-(CTA, rank)
+    # done flags (148 CTAs).
+    def expect(rows, hidden, world):
+        r256 = lambda x: (x + 255) // 256 * 256
+        tiles = -(-rows // 128) * (hidden // 256)
+        grid = min(tiles, 148)
+        rounds = -(-tiles // grid)
+        slots = -(-rounds // world) * grid
+        total = r256(rows * hidden * 2)
+        if world > 1:
+            total += slots * world * 128 * 512 + r256(tiles * world * 16) + r256(148 * world * 4)
+        return total
+    for rows, hidden, world in [(16384, 2048, 2), (65536, 2048, 8), (8192, 2048, 1),
+                                (100, 1024, 4), (32768, 2048, 4)]:
+        assert G.tail_exchange_bytes(rows, hidden, world) == expect(rows, hidden, world)
+    assert G.tail_exchange_bytes(128, 1000, 2) == 0
+    assert G.tail_exchange_bytes(128, 2048, 3) == 0
+    assert G.tail_exchange_bytes(0, 2048, 2) == 0
+    assert G.output_tail_allreduce_workspace_bytes(100, 16) == 256 + 100 * 16 * 128 * 2
+
+
+def test_exchange_entry_points_without_gpu_fail_loudly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    region = ctypes.c_void_p()
+    assert lib().gdn_b200_exchange_alloc(1 << 20, ctypes.byref(region)) == G.INTERNAL
+    assert region.value is None
+    assert tail_ar(_group()) == G.INTERNAL
+    assert lib().gdn_b200_exchange_export(None, None) == G.INVALID_ARGUMENT

@@ -1,0 +1,143 @@
+"""Head-parallel output tail with the rank sum fused into the tail GEMM
+(``gdn_b200_output_tail_allreduce``).
+
+* World size 1 (one GPU): no exchange; the fused kernel's epilogue (staged
+  through shared memory, row-contiguous stores) must give the same bits as
+  the single-GPU tail.
+* World size 2 (two GPUs, one process each, exchange regions mapped by CUDA
+  IPC): both ranks must hold the same bits, within the output tolerance of
+  the full-width tail (the oracle's, or the single-GPU kernel's at full
+  size), over several calls in a row (growing epochs).
+
+Tolerances: max |gpu - ref| <= 2e-2 and mean|gpu - ref| / mean|ref| <= 5e-3.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import gdn_b200 as G
+import gdn_oracle as O
+
+OUT_MAX_ABS = 2e-2
+OUT_MEAN_REL = 5e-3
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(rows, hv, hidden, seed=0):
+    D = G.HEAD_DIM
+    return dict(o=G.fill(seed, 41, (rows, hv, D), G.NORMAL, 0.0, 1.0, G.BF16),
+                z=G.fill(seed, 42, (rows, hv, D), G.NORMAL, 0.0, 1.0, G.BF16),
+                gamma=G.fill(seed, 43, (D,), G.NORMAL, 1.0, 0.02, G.BF16),
+                w=G.fill(seed, 44, (hidden, hv * D), G.NORMAL, 0.0, 0.02, G.BF16))
+
+
+def _assert_close(gpu_bits, ref_bits, what):
+    g = O.bf16_to_f32(gpu_bits).astype(np.float64)
+    r = O.bf16_to_f32(ref_bits).astype(np.float64)
+    d = np.abs(g - r)
+    mx, mr = float(d.max()), float(d.mean() / max(np.abs(r).mean(), 1e-30))
+    assert mx <= OUT_MAX_ABS and mr <= OUT_MEAN_REL, f"{what}: max_abs={mx:.3e} mean_rel={mr:.3e}"
+
+
+@pytest.mark.parametrize("rows,hv,hidden,max_rows", [(8192, 32, 2048, 8192),
+                                                     (1000, 8, 1024, 1000),
+                                                     (130, 16, 2048, 4096),
+                                                     (1, 4, 256, 1)])
+def test_world1_matches_single_gpu_tail_bits(cuda, rows, hv, hidden, max_rows):
+    import torch
+    x = _inputs(rows, hv, hidden)
+    t = G.to_device(x, cuda)
+    ref = G.bf16_bits(G.output_tail(t["o"], t["z"], t["gamma"], t["w"]))
+    grp = G.TailGroup(max_rows, hidden, 0, 1, cuda)
+    try:
+        ws = torch.empty(G.output_tail_allreduce_workspace_bytes(rows, hv), dtype=torch.uint8,
+                         device=cuda)
+        for _ in range(2):
+            out = grp.output_tail(t["o"], t["z"], t["gamma"], t["w"], workspace=ws)
+            G.workspace_status(ws)
+            assert np.array_equal(G.bf16_bits(out), ref), "fused tail (world 1) differs"
+        if rows <= 1000:
+            _assert_close(G.bf16_bits(out), O.output_tail(x["o"], x["z"], x["gamma"], x["w"]),
+                          f"world 1 rows={rows}")
+    finally:
+        torch.cuda.synchronize()
+        grp.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, rows, hv_total, hidden, calls, outdir):
+    """One rank: its share of the heads and of w_out's columns, the fused tail
+    `calls` times, then its output bits (and, at rank 0, the single-GPU
+    full-width tail) written to `outdir`."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=120))
+    try:
+        x = _inputs(rows, hv_total, hidden)
+        hv = hv_total // world
+        K = hv * G.HEAD_DIM
+        mine = dict(o=np.ascontiguousarray(x["o"][:, rank * hv:(rank + 1) * hv]),
+                    z=np.ascontiguousarray(x["z"][:, rank * hv:(rank + 1) * hv]),
+                    gamma=x["gamma"],
+                    w=np.ascontiguousarray(x["w"][:, rank * K:(rank + 1) * K]))
+        t = G.to_device(mine, dev)
+
+        def exchange(payload):
+            got = [None] * world
+            dist.all_gather_object(got, payload)
+            return got
+
+        grp = G.TailGroup(rows, hidden, rank, world, dev, exchange=exchange)
+        ws = torch.empty(G.output_tail_allreduce_workspace_bytes(rows, hv), dtype=torch.uint8,
+                         device=dev)
+        stream = torch.cuda.Stream(device=dev)
+        for _ in range(calls):
+            out = grp.output_tail(t["o"], t["z"], t["gamma"], t["w"], workspace=ws,
+                                  stream=stream)
+        G.workspace_status(ws, stream)
+        np.save(os.path.join(outdir, f"rank{rank}.npy"), G.bf16_bits(out))
+        if rank == 0:
+            full = G.to_device(x, dev)
+            ref = G.output_tail(full["o"], full["z"], full["gamma"], full["w"])
+            np.save(os.path.join(outdir, "single.npy"), G.bf16_bits(ref))
+        torch.cuda.synchronize()
+        dist.barrier()
+        grp.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("rows,hv_total,hidden,calls", [(1000, 32, 2048, 3),
+                                                        (16384, 32, 2048, 4),
+                                                        (200, 8, 512, 2)])
+def test_world2_ranks_agree_and_match_full_tail(cuda, tmp_path, rows, hv_total, hidden, calls):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_rank_main, args=(2, _free_port(), rows, hv_total, hidden, calls,
+                                         str(tmp_path)),
+                       nprocs=2, start_method="spawn")
+    r0 = np.load(tmp_path / "rank0.npy")
+    r1 = np.load(tmp_path / "rank1.npy")
+    single = np.load(tmp_path / "single.npy")
+    assert r0.shape == (rows, hidden)
+    assert np.array_equal(r0, r1), "ranks hold different outputs"
+    _assert_close(r0, single, f"world 2 vs single-GPU rows={rows}")
+    if rows <= 1000:
+        x = _inputs(rows, hv_total, hidden)
+        _assert_close(r0, O.output_tail(x["o"], x["z"], x["gamma"], x["w"]),
+                      f"world 2 vs oracle rows={rows}")

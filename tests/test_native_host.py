@@ -54,6 +54,7 @@ def test_provider_abi_layout_matches_python_mirror(tmp_path):
         "statecentric_qwen38_error_v1": G.ErrorV1,
         "statecentric_qwen38_completion_v1": G.CompletionV1,
         "statecentric_qwen38_provider_descriptor_v1": G.DescriptorV1,
+        "gdn_b200_tail_group_v1": G.TailGroupV1,
     }
     for key, value in c_layout.items():
         if key == "MIN_SIZE":
