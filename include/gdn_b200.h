@@ -152,9 +152,9 @@ GDN_B200_API int32_t gdn_b200_layer_forward(const void* q, const void* k, const 
  * point (no counterpart in the reference) sums it inside the tail GEMM
  * kernel over NVLink peer memory, tile by tile, and leaves the full output
  * on every rank:
- *   out = bf16( f32(owning rank's partial) + sum over the other ranks, in
- *               rank order, of bf16(their partial) ),
- * the same bits on every rank.
+ *   out = bf16( sum over ranks, in rank order, in f32, of bf16(partial) ),
+ * the same bits on every rank (a bf16 all-reduce of the rank-partial outputs
+ * with f32 accumulation).
  *
  * Each rank owns an exchange region of gdn_b200_tail_exchange_bytes bytes
  * (gdn_b200_exchange_alloc: zero-filled device memory of the current

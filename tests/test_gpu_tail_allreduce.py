@@ -3,13 +3,23 @@
 
 * World size 1 (one GPU): no exchange; the fused kernel's epilogue (staged
   through shared memory, row-contiguous stores) must give the same bits as
-  the single-GPU tail.
+  the single-GPU tail wherever that one does not split K.
 * World size 2 (two GPUs, one process each, exchange regions mapped by CUDA
-  IPC): both ranks must hold the same bits, within the output tolerance of
-  the full-width tail (the oracle's, or the single-GPU kernel's at full
-  size), over several calls in a row (growing epochs).
+  IPC), over several calls in a row (growing epochs): both ranks must hold
+  the same bits, equal to the sum of the ranks' bf16 partial tails (each
+  rank's tail over its own heads from the same GEMM main loop, added in f32
+  in rank order and rounded: what the reference's engine gets from the
+  rank-partial outputs, P:3541-3547, with a bf16 all-reduce); against the
+  single-GPU full-width tail every element must be within the rounding a
+  bf16 rank sum may add; and the output must meet the tolerance below
+  against the oracle's full-width tail (small cases) and in the mean against
+  the single-GPU tail.
 
 Tolerances: max |gpu - ref| <= 2e-2 and mean|gpu - ref| / mean|ref| <= 5e-3.
+A bf16 rank sum adds up to one bf16 ulp to the result (0.03 for outputs of
+magnitude 4 to 8), so against the full-size single-GPU tail the maximum is
+bounded element by element instead (half an ulp of each partial + one ulp of
+the result).
 """
 import os
 import socket
@@ -42,11 +52,40 @@ def _assert_close(gpu_bits, ref_bits, what):
     assert mx <= OUT_MAX_ABS and mr <= OUT_MEAN_REL, f"{what}: max_abs={mx:.3e} mean_rel={mr:.3e}"
 
 
+def _bf16_ulp(bits):
+    """Spacing of bf16 numbers at each value (bf16 keeps 8 of f32's 24
+    significand bits)."""
+    return np.spacing(np.abs(O.bf16_to_f32(bits)).astype(np.float32)).astype(np.float64) * 65536.0
+
+
+def _assert_rank_sum_bound(gpu_bits, ref_bits, partials, what):
+    """|gpu - ref| <= half a bf16 ulp of every rank partial (the rounding a
+    bf16 rank sum may apply to each) + one ulp of the result (the final
+    roundings).  Relative to the result this is loose only where the
+    partials cancel."""
+    g = O.bf16_to_f32(gpu_bits).astype(np.float64)
+    r = O.bf16_to_f32(ref_bits).astype(np.float64)
+    bound = 0.5 * sum(_bf16_ulp(p) for p in partials)
+    bound = bound + np.maximum(_bf16_ulp(gpu_bits), _bf16_ulp(ref_bits))
+    # f32 accumulation-order differences between kernels (K <= 4096)
+    bound = bound + 2.0 ** -20 * sum(np.abs(O.bf16_to_f32(p)).astype(np.float64)
+                                     for p in partials)
+    bad = np.abs(g - r) > bound
+    assert not bad.any(), f"{what}: {int(bad.sum())} elements beyond the rank-sum bound"
+
+
+def _single_gpu_tail_splits_k(rows, hidden):
+    """The single-GPU tail splits K over CTAs (another f32 summation order)
+    when it has fewer than 75 output tiles."""
+    return -(-rows // 128) * (hidden // 256) * 2 <= 148
+
+
 @pytest.mark.parametrize("rows,hv,hidden,max_rows", [(8192, 32, 2048, 8192),
+                                                     (4000, 16, 2048, 4096),
                                                      (1000, 8, 1024, 1000),
                                                      (130, 16, 2048, 4096),
                                                      (1, 4, 256, 1)])
-def test_world1_matches_single_gpu_tail_bits(cuda, rows, hv, hidden, max_rows):
+def test_world1_matches_single_gpu_tail(cuda, rows, hv, hidden, max_rows):
     import torch
     x = _inputs(rows, hv, hidden)
     t = G.to_device(x, cuda)
@@ -58,7 +97,10 @@ def test_world1_matches_single_gpu_tail_bits(cuda, rows, hv, hidden, max_rows):
         for _ in range(2):
             out = grp.output_tail(t["o"], t["z"], t["gamma"], t["w"], workspace=ws)
             G.workspace_status(ws)
-            assert np.array_equal(G.bf16_bits(out), ref), "fused tail (world 1) differs"
+            if _single_gpu_tail_splits_k(rows, hidden):
+                _assert_close(G.bf16_bits(out), ref, f"world 1 vs single-GPU rows={rows}")
+            else:
+                assert np.array_equal(G.bf16_bits(out), ref), "fused tail (world 1) differs"
         if rows <= 1000:
             _assert_close(G.bf16_bits(out), O.output_tail(x["o"], x["z"], x["gamma"], x["w"]),
                           f"world 1 rows={rows}")
@@ -109,6 +151,14 @@ def _rank_main(rank, world, port, rows, hv_total, hidden, calls, outdir):
                                   stream=stream)
         G.workspace_status(ws, stream)
         np.save(os.path.join(outdir, f"rank{rank}.npy"), G.bf16_bits(out))
+        # This rank's bf16 partial from the same GEMM main loop (a one-rank
+        # group), i.e. exactly what the exchange rounded and sent.
+        solo = G.TailGroup(rows, hidden, 0, 1, dev)
+        partial = solo.output_tail(t["o"], t["z"], t["gamma"], t["w"], workspace=ws,
+                                   stream=stream)
+        G.workspace_status(ws, stream)
+        np.save(os.path.join(outdir, f"partial{rank}.npy"), G.bf16_bits(partial))
+        solo.close()
         if rank == 0:
             full = G.to_device(x, dev)
             ref = G.output_tail(full["o"], full["z"], full["gamma"], full["w"])
@@ -136,7 +186,13 @@ def test_world2_ranks_agree_and_match_full_tail(cuda, tmp_path, rows, hv_total, 
     single = np.load(tmp_path / "single.npy")
     assert r0.shape == (rows, hidden)
     assert np.array_equal(r0, r1), "ranks hold different outputs"
-    _assert_close(r0, single, f"world 2 vs single-GPU rows={rows}")
+    partials = [np.load(tmp_path / f"partial{r}.npy") for r in range(2)]
+    rank_sum = O.f32_to_bf16(O.bf16_to_f32(partials[0]) + O.bf16_to_f32(partials[1]))
+    assert np.array_equal(r0, rank_sum), "fused sum differs from the bf16 rank sum"
+    _assert_rank_sum_bound(r0, single, partials, f"world 2 vs single-GPU rows={rows}")
+    g = O.bf16_to_f32(r0).astype(np.float64)
+    ref = O.bf16_to_f32(single).astype(np.float64)
+    assert np.abs(g - ref).mean() / np.abs(ref).mean() <= OUT_MEAN_REL
     if rows <= 1000:
         x = _inputs(rows, hv_total, hidden)
         _assert_close(r0, O.output_tail(x["o"], x["z"], x["gamma"], x["w"]),
