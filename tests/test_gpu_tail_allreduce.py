@@ -4,7 +4,7 @@
 * World size 1 (one GPU): no exchange; the fused kernel's epilogue (staged
   through shared memory, row-contiguous stores) must give the same bits as
   the single-GPU tail wherever that one does not split K.
-* World size 2 (two GPUs, one process each, exchange regions mapped by CUDA
+* World sizes 2, 4 and 8 (one process per GPU, exchange regions mapped by CUDA
   IPC), over several calls in a row (growing epochs): both ranks must hold
   the same bits, equal to the sum of the ranks' bf16 partial tails (each
   rank's tail over its own heads from the same GEMM main loop, added in f32
@@ -170,30 +170,38 @@ def _rank_main(rank, world, port, rows, hv_total, hidden, calls, outdir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("rows,hv_total,hidden,calls", [(1000, 32, 2048, 3),
-                                                        (16384, 32, 2048, 4),
-                                                        (200, 8, 512, 2)])
-def test_world2_ranks_agree_and_match_full_tail(cuda, tmp_path, rows, hv_total, hidden, calls):
+@pytest.mark.parametrize("world,rows,hv_total,hidden,calls", [(2, 1000, 32, 2048, 3),
+                                                              (2, 16384, 32, 2048, 4),
+                                                              (2, 200, 8, 512, 2),
+                                                              (4, 1000, 32, 2048, 3),
+                                                              (4, 32768, 32, 2048, 2),
+                                                              (8, 1000, 32, 2048, 3),
+                                                              (8, 8192, 32, 2048, 2)])
+def test_ranks_agree_and_match_full_tail(cuda, tmp_path, world, rows, hv_total, hidden, calls):
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    mp.start_processes(_rank_main, args=(2, _free_port(), rows, hv_total, hidden, calls,
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_rank_main, args=(world, _free_port(), rows, hv_total, hidden, calls,
                                          str(tmp_path)),
-                       nprocs=2, start_method="spawn")
-    r0 = np.load(tmp_path / "rank0.npy")
-    r1 = np.load(tmp_path / "rank1.npy")
+                       nprocs=world, start_method="spawn")
+    outs = [np.load(tmp_path / f"rank{r}.npy") for r in range(world)]
+    r0 = outs[0]
     single = np.load(tmp_path / "single.npy")
     assert r0.shape == (rows, hidden)
-    assert np.array_equal(r0, r1), "ranks hold different outputs"
-    partials = [np.load(tmp_path / f"partial{r}.npy") for r in range(2)]
-    rank_sum = O.f32_to_bf16(O.bf16_to_f32(partials[0]) + O.bf16_to_f32(partials[1]))
+    for r in range(1, world):
+        assert np.array_equal(r0, outs[r]), f"rank {r} holds a different output"
+    partials = [np.load(tmp_path / f"partial{r}.npy") for r in range(world)]
+    acc = O.bf16_to_f32(partials[0]).astype(np.float32)
+    for part in partials[1:]:
+        acc = acc + O.bf16_to_f32(part)
+    rank_sum = O.f32_to_bf16(acc)
     assert np.array_equal(r0, rank_sum), "fused sum differs from the bf16 rank sum"
-    _assert_rank_sum_bound(r0, single, partials, f"world 2 vs single-GPU rows={rows}")
+    _assert_rank_sum_bound(r0, single, partials, f"world {world} vs single-GPU rows={rows}")
     g = O.bf16_to_f32(r0).astype(np.float64)
     ref = O.bf16_to_f32(single).astype(np.float64)
     assert np.abs(g - ref).mean() / np.abs(ref).mean() <= OUT_MEAN_REL
     if rows <= 1000:
         x = _inputs(rows, hv_total, hidden)
         _assert_close(r0, O.output_tail(x["o"], x["z"], x["gamma"], x["w"]),
-                      f"world 2 vs oracle rows={rows}")
+                      f"world {world} vs oracle rows={rows}")
