@@ -7,7 +7,7 @@
 // to 8-token recurrent slices (run_sequence, P:3387-3469).  Here every chunk
 // of every sequence is processed in two launches.
 //
-// 1. gdn_chunk_prep_kernel: chunk-parallel and persistent (two CTAs per SM,
+// 1. gdn_chunk_prep_kernel: chunk-parallel and persistent (three CTAs per SM,
 //    units of one chunk x one q/k head, the next unit's q/k tile on its way
 //    by TMA), everything that does not depend on the recurrent state:
 //      q, k L2-norm -> the bf16 [K;Q] operand image (shared by the v-heads),
@@ -79,7 +79,7 @@ __device__ __forceinline__ void group_barrier(int id, int threads) {
 // for every column and all trip counts are compile-time constants.
 // Thread u -> column cc = u % (16 I) and rows r0 + k * rstep.
 template <int I>
-__device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], float (*X)[52],
+__device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], float (*X)[49],
                                                 int u, int grp, bool live) {
   constexpr int kCols = 16 * I;
   constexpr int kStep = 128 / kCols;              // 8, 4, 2
@@ -89,23 +89,32 @@ __device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], 
   const bool worker = live && r0 < kStep;
   float acc[kRows];
   if (worker) {
-    float tcol[kCols];
+    // Column cc of T in 16-row pieces (keeps the register count low enough
+    // for three CTAs per SM).
+    float a0[kRows], a1[kRows];
 #pragma unroll
-    for (int m = 0; m < kCols; ++m) tcol[m] = T[m][cc];
+    for (int k = 0; k < kRows; ++k) a0[k] = a1[k] = 0.f;
 #pragma unroll
-    for (int k = 0; k < kRows; ++k) {
-      const int rr = r0 + k * kStep;
-      float a0 = 0.f, a1 = 0.f;
+    for (int m0 = 0; m0 < kCols; m0 += 16) {
+      float tcol[16];
 #pragma unroll
-      for (int m = 0; m < kCols; m += 4) {
-        const float4 av = *reinterpret_cast<const float4*>(&A[16 * I + rr][m]);
-        a0 += av.x * tcol[m] + av.y * tcol[m + 1];
-        a1 += av.z * tcol[m + 2] + av.w * tcol[m + 3];
+      for (int m = 0; m < 16; ++m) tcol[m] = T[m0 + m][cc];
+#pragma unroll
+      for (int k = 0; k < kRows; ++k) {
+        const int rr = r0 + k * kStep;
+#pragma unroll
+        for (int m = 0; m < 16; m += 4) {
+          const float4 av = *reinterpret_cast<const float4*>(&A[16 * I + rr][m0 + m]);
+          a0[k] += av.x * tcol[m] + av.y * tcol[m + 1];
+          a1[k] += av.z * tcol[m + 2] + av.w * tcol[m + 3];
+        }
       }
-      acc[k] = a0 + a1;
     }
 #pragma unroll
-    for (int k = 0; k < kRows; ++k) X[r0 + k * kStep][cc] = acc[k];
+    for (int k = 0; k < kRows; ++k) {
+      acc[k] = a0[k] + a1[k];
+      X[r0 + k * kStep][cc] = acc[k];
+    }
   }
   group_barrier(1 + grp, 128);
   if (worker) {
@@ -137,24 +146,28 @@ __device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], 
 constexpr int kPrepThreads = 256;
 
 struct PrepSmem {
-  uint8_t kq[2][kKQBytes];  // [K;Q] tiles of two units (1024-aligned): raw q/k land
-                            // here by TMA and are normalised in place
+  uint8_t kq[kKQBytes];     // [K;Q] tile (1024-aligned): raw q/k land here by TMA
+                            // and are normalised in place
   float amat[2][64][68];    // A, overwritten in place by T = (I + A)^-1
-  float xs[2][16][52];      // block-merge temporaries
+  float xs[2][16][49];      // block-merge temporaries (odd stride: no bank conflicts)
   float g[2][64];           // cumsum G
   float e1[2][64];          // exp(g_t) = exp(G_t - G_{t-1})
   float beta[2][64];
   float carry[2];
-  uint64_t full[2];         // raw tile of the unit in kq[i] has landed
+  uint64_t full;            // raw tile of the current unit has landed
   uint64_t mma;             // [K;Q] K^T of the current unit has completed
   uint32_t tmem;
 };
+// Three CTAs per SM: 3 x (this + 1 KB alignment slack + 1 KB reserved) must
+// fit in the SM's 228 KB.
+static_assert(sizeof(PrepSmem) + 1024 <= 228 * 1024 / 3 - 1024, "prep shared memory");
 
 // Persistent: CTA x handles units x, x + gridDim.x, ... (unit = chunk * Hk +
-// q/k head).  While one unit is processed, the raw q/k tile of the next one
-// is already on its way into the other buffer, and the finished [K;Q] image
-// goes back to global memory as one bulk store.
-__global__ void __launch_bounds__(kPrepThreads, 2)
+// q/k head).  The finished [K;Q] image goes back to global memory as one bulk
+// store; once that store and the unit's MMA have read the tile buffer, the
+// raw q/k tile of the next unit is loaded into it by TMA while the rest of the
+// unit (A, P and the inverse, most of its time) runs.  Three CTAs per SM.
+__global__ void __launch_bounds__(kPrepThreads, 3)
 gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
                       const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k,
@@ -176,27 +189,26 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
 
   // Raw q/k tile of a unit: K rows 0-63 and Q rows 64-127 of both 64-column
   // slabs, four 8 KB boxes (tokens past the tensor read as zero).
-  auto load_unit = [&](int unit, int buf) {
+  auto load_unit = [&](int unit) {
     const int chunk = unit / qk_heads;
     const int kh = unit - chunk * qk_heads;
     const int seq = find_seq(tab, chunk);
     const int t0 = tab.cu[seq] + (chunk - tab.chunk_start[seq]) * kChunk;
-    uint8_t* dst = sm.kq[buf];
-    mbar_arrive_expect_tx(&sm.full[buf], kKQBytes);
-    tma_load_3d(dst, &tm_k, &sm.full[buf], 0, kh, t0);
-    tma_load_3d(dst + 16384, &tm_k, &sm.full[buf], 64, kh, t0);
-    tma_load_3d(dst + 8192, &tm_q, &sm.full[buf], 0, kh, t0);
-    tma_load_3d(dst + 16384 + 8192, &tm_q, &sm.full[buf], 64, kh, t0);
+    uint8_t* dst = sm.kq;
+    mbar_arrive_expect_tx(&sm.full, kKQBytes);
+    tma_load_3d(dst, &tm_k, &sm.full, 0, kh, t0);
+    tma_load_3d(dst + 16384, &tm_k, &sm.full, 64, kh, t0);
+    tma_load_3d(dst + 8192, &tm_q, &sm.full, 0, kh, t0);
+    tma_load_3d(dst + 16384 + 8192, &tm_q, &sm.full, 64, kh, t0);
   };
 
   if (threadIdx.x == 0) {
-    mbar_init(&sm.full[0], 1);
-    mbar_init(&sm.full[1], 1);
+    mbar_init(&sm.full, 1);
     mbar_init(&sm.mma, 1);
     fence_barrier_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
-    if (static_cast<int>(blockIdx.x) < units) load_unit(blockIdx.x, 0);
+    if (static_cast<int>(blockIdx.x) < units) load_unit(blockIdx.x);
   }
   if (warp == 0) tmem_alloc(&sm.tmem, 64);
   tmem_fence_before();
@@ -206,7 +218,6 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
 
   int it = 0;
   for (int unit = blockIdx.x; unit < units; unit += gridDim.x, ++it) {
-    const int buf = it & 1;
     const int chunk = unit / qk_heads;
     const int kh = unit - chunk * qk_heads;
     const int seq = find_seq(tab, chunk);
@@ -229,23 +240,24 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
     // bf16, in place.  Two threads per row (row r = tid / 2, half = tid % 2:
     // the 64-column slab `half`, eight 16-byte chunks); rows past the chunk
     // are zeroed.
-    bool landed = mbar_wait(&sm.full[buf], (it >> 1) & 1, err);
+    bool landed = mbar_wait(&sm.full, it & 1, err);
     {
-      uint8_t* tile = sm.kq[buf];
+      uint8_t* tile = sm.kq;
       const float l2gamma = round_bf16(0.08838834764831845f);
       const int r = threadIdx.x >> 1;
       const int half = threadIdx.x & 1;
       const int tok = r & 63;
-      uint4 raw[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        raw[c] = (landed && tok < n)
-                     ? *reinterpret_cast<const uint4*>(tile + half * 16384u + sw128_chunk(r, c))
-                     : make_uint4(0u, 0u, 0u, 0u);
+      // Two passes over the row's chunks (sum of squares, then scale): the
+      // tile is read twice from shared memory instead of being held in
+      // registers.
+      const bool live_row = landed && tok < n;
       float ss = 0.f;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+        const uint4 v = live_row
+                            ? *reinterpret_cast<const uint4*>(tile + half * 16384u + sw128_chunk(r, c))
+                            : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
           const float x0 = bf16lo_f32(w[p]), x1 = bf16hi_f32(w[p]);
@@ -256,7 +268,10 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
       const float rs = rsqrtf(ss * (1.0f / 128.0f) + 1.0e-6f / 128.0f) * l2gamma;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+        const uint4 v = live_row
+                            ? *reinterpret_cast<const uint4*>(tile + half * 16384u + sw128_chunk(r, c))
+                            : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint4 o;
         o.x = pack_bf16x2(bf16lo_f32(w[0]) * rs, bf16hi_f32(w[0]) * rs);
         o.y = pack_bf16x2(bf16lo_f32(w[1]) * rs, bf16hi_f32(w[1]) * rs);
@@ -273,7 +288,7 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
     if (threadIdx.x == 0) {
       // D[128 x 64] = [K;Q] K^T: lanes 0-63 hold K K^T, lanes 64-127 Q K^T.
       constexpr uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
-      const uint32_t t = smem_u32(sm.kq[buf]);
+      const uint32_t t = smem_u32(sm.kq);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t off = (kk >> 2) * 16384u + (kk & 3) * 32u;
@@ -282,15 +297,8 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
       }
       umma_commit(&sm.mma);
       // The [K;Q] image to its record.
-      bulk_store(kq_records + static_cast<int64_t>(unit) * kKQBytes, sm.kq[buf], kKQBytes);
+      bulk_store(kq_records + static_cast<int64_t>(unit) * kKQBytes, sm.kq, kKQBytes);
       bulk_commit();
-      // Next unit into the other buffer, once the previous unit's store has
-      // read it (its MMA completed during the previous unit).
-      const int next = unit + gridDim.x;
-      if (next < units) {
-        bulk_wait_read<1>();
-        load_unit(next, buf ^ 1);
-      }
     }
 
     bool ok = true;
@@ -299,7 +307,7 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
     // I of T is formed, and T's strictly upper part equals A's (zero).
     float (*A)[68] = sm.amat[grp];
     float (*T)[68] = sm.amat[grp];
-    float (*X)[52] = sm.xs[grp];
+    float (*X)[49] = sm.xs[grp];
 
     for (int hp = 0; hp < group; hp += 2) {
       const int hl = hp + grp;
@@ -357,14 +365,8 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
       }
       tmem_fence_after();
       if (active && ok) {
+        // TMEM row of this lane, 16 columns at a time.
         const uint32_t base = tmem_addr(tmem, quarter * 32, 0);
-        uint32_t r[64];
-  #pragma unroll
-        for (int c = 0; c < 64; c += 16) {
-          uint32_t* rc = r + c;
-          tmem_ld16(base + c, *reinterpret_cast<uint32_t(*)[16]>(rc));
-        }
-        tmem_ld_wait();
         if (u < 64) {
           // Lane u holds row u of K K^T = column u (symmetric).  Column u of A:
           // A[i][u] = beta_i KK_iu exp(G_i - G_u) for u < i < n, with the decay
@@ -374,6 +376,8 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
           float d = 1.f;
   #pragma unroll
           for (int c = 0; c < 64; c += 16) {
+            uint32_t r[16];
+            tmem_ld16(base + c, r);
             float e1v[16], bv[16];
   #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
@@ -382,46 +386,55 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
               e1v[4 * q4] = ev.x; e1v[4 * q4 + 1] = ev.y; e1v[4 * q4 + 2] = ev.z; e1v[4 * q4 + 3] = ev.w;
               bv[4 * q4] = bb.x; bv[4 * q4 + 1] = bb.y; bv[4 * q4 + 2] = bb.z; bv[4 * q4 + 3] = bb.w;
             }
-            float col[16];
+            tmem_ld_wait();
   #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int i = c + j;
               d = (i > u) ? d * e1v[j] : 1.f;
-              col[j] = (i > u && i < n) ? bv[j] * __uint_as_float(r[i]) * d : 0.f;
+              A[i][u] = (i > u && i < n) ? bv[j] * __uint_as_float(r[j]) * d : 0.f;
             }
-  #pragma unroll
-            for (int j = 0; j < 16; ++j) A[c + j][u] = col[j];
           }
         } else {
           // Lane 64+i holds row i of Q K^T: P[i][j] = QK_ij exp(G_i - G_j),
-          // j <= i < n, decay as a running product towards smaller j.
+          // j <= i < n, decay as a running product towards smaller j; each
+          // 16-column piece goes to the record as two 16-byte chunks.
           const int i = u - 64;
           float d = 1.f;
-          uint32_t w[32];
   #pragma unroll
           for (int c = 48; c >= 0; c -= 16) {
+            uint32_t r[16];
+            tmem_ld16(base + c, r);
             float e1v[16];
   #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
               const float4 ev = *reinterpret_cast<const float4*>(&sm.e1[grp][c + 4 * q4]);
               e1v[4 * q4] = ev.x; e1v[4 * q4 + 1] = ev.y; e1v[4 * q4 + 2] = ev.z; e1v[4 * q4 + 3] = ev.w;
             }
+            tmem_ld_wait();
+            uint32_t w[8];
   #pragma unroll
             for (int jj = 15; jj >= 0; --jj) {
               const int j = c + jj;
-              const float pj = (j <= i && i < n) ? __uint_as_float(r[j]) * d : 0.f;
+              const float pj = (j <= i && i < n) ? __uint_as_float(r[jj]) * d : 0.f;
               d = (j <= i) ? d * e1v[jj] : 1.f;
-              if (j & 1) w[j >> 1] = __float_as_uint(pj);
-              else w[j >> 1] = pack_bf16x2(pj, __uint_as_float(w[j >> 1]));
+              if (jj & 1) w[jj >> 1] = __float_as_uint(pj);
+              else w[jj >> 1] = pack_bf16x2(pj, __uint_as_float(w[jj >> 1]));
             }
+            *reinterpret_cast<uint4*>(rec + kRecP + sw128_chunk(i, c >> 3)) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(rec + kRecP + sw128_chunk(i, (c >> 3) + 1)) =
+                make_uint4(w[4], w[5], w[6], w[7]);
           }
-  #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(rec + kRecP + sw128_chunk(i, c)) =
-                make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
         }
       }
       group_barrier(1 + grp, 128);
+      if (hp == 0 && threadIdx.x == 0) {
+        // The unit's MMA and [K;Q] store have read the tile buffer (the MMA
+        // was waited for above): the next unit's tile can land in it now.
+        bulk_wait_read<0>();
+        const int next = unit + gridDim.x;
+        if (next < units) load_unit(next);
+      }
 
       // T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution
       // (one thread per block column), then block rows I = 1..3:
@@ -1044,18 +1057,18 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
   cudaError_t e = cudaFuncSetAttribute(gdn_chunk_prep_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem);
   if (e != cudaSuccess) return e;
-  // All of L1 as shared memory, so that two CTAs fit on an SM.
+  // All of L1 as shared memory, so that three CTAs fit on an SM.
   e = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                            100);
   if (e != cudaSuccess) return e;
-  // Persistent grid: two CTAs per SM (128 registers x 256 threads and about
-  // 100 KB of shared memory each), at most one per unit.  CTAs never wait on
-  // one another, so fewer resident slots only means a second wave.
+  // Persistent grid: three CTAs per SM (at most 85 registers x 256 threads and
+  // about 75 KB of shared memory each), at most one per unit.  CTAs never
+  // wait on one another, so fewer resident slots only means a second wave.
   int device = 0, sms = 0;
   if ((e = cudaGetDevice(&device)) != cudaSuccess) return e;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return e;
   const int64_t units = static_cast<int64_t>(tab.total_chunks) * qk_heads;
-  const int pgrid = static_cast<int>(std::min<int64_t>(units, 2 * static_cast<int64_t>(sms)));
+  const int pgrid = static_cast<int>(std::min<int64_t>(units, 3 * static_cast<int64_t>(sms)));
   gdn_chunk_prep_kernel<<<pgrid, kPrepThreads, prep_smem, stream>>>(
       tab, tq, tk, a, b, A_log, dt_bias, kq_records, records, qk_heads, value_heads, err);
   e = cudaGetLastError();
