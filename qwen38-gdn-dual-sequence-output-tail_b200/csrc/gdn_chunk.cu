@@ -599,10 +599,10 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
     mbar_init(mma_bar, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&stage_free[i], 1);
-      mbar_init(&tile_ready[i], kComputeThreads);
+      mbar_init(&tile_ready[i], kComputeThreads / 32);
       mbar_init(&tile_free[i], 1);
     }
-    mbar_init(rdy, kComputeThreads);
+    mbar_init(rdy, kComputeThreads / 32);
     fence_barrier_init();
   }
   if (warp == 0) tmem_alloc(tmem_slot, 512);
@@ -782,10 +782,13 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
       tmem_fence_after();
       return r;
     };
+    // One arrival per compute warp (after every lane's fences and a warp
+    // barrier): 8 arrivals instead of 256 on the same mbarrier word.
     auto ready = [&]() {
       fence_proxy_async_smem();
       tmem_fence_before();
-      mbar_arrive(rdy);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(rdy);
     };
 
     // State: thread owns key row lrow, value columns dvh*64 + c0 + [0, 32).
@@ -868,7 +871,8 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
         tmem_fence_after();
         write_output(d1_prev, (c - 1) & 1, kChunk);
         fence_proxy_async_smem();
-        mbar_arrive(&tile_ready[(c - 1) & 1]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tile_ready[(c - 1) & 1]);
       }
       if (!mbar_wait(&full[st], (c >> 1) & 1, err) || !wait_mma()) { ok = false; break; }
 
@@ -963,7 +967,8 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
         write_output(tmem + kTmD1 + ((nchunks - 1) & 1) * 128, (nchunks - 1) & 1, last_n);
         if (last_n == kChunk) {
           fence_proxy_async_smem();
-          mbar_arrive(&tile_ready[(nchunks - 1) & 1]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tile_ready[(nchunks - 1) & 1]);
         }
       }
 #pragma unroll
