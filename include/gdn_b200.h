@@ -142,6 +142,52 @@ GDN_B200_API int32_t gdn_b200_layer_forward(const void* q, const void* k, const 
                                uint64_t workspace_bytes, void* stream);
 
 /* ----------------------------------------------------------------------
+ * Input side of the layer: x -> q, k, v, z, a, b.  Replaces the reference's
+ * projections (four aclnnMatmul calls, P:3101-3130), aclnnCausalConv1d with
+ * the conv-state update (P:3132-3179) and the Q/K/V split (P:3186-3247).
+ *   x        bf16 [T, hidden]   the normalised layer input (reference input 0)
+ *   w_qkv    bf16 [(2 Hk + Hv) 128, hidden], w_z bf16 [Hv 128, hidden],
+ *   w_a, w_b bf16 [Hv, hidden]  (reference inputs 1-4: dims {hidden, N},
+ *                               strides {1, hidden})
+ *   conv_w   bf16 [4, (2 Hk + Hv) 128]   (input 5: tap k multiplies x[t-3+k])
+ *   conv_state bf16 [S, 3, (2 Hk + Hv) 128]  (region gdn.conv: the last three
+ *            projected rows of each sequence), updated in place; with
+ *            use_conv_state = 0 the history is taken as zero (a submission
+ *            without context) and the state is still written.
+ * q, k, v are the conv output (SiLU applied) split at Hk 128 and 2 Hk 128;
+ * z, a, b are the projections.  L2-norm and gating follow in the layer. */
+GDN_B200_API uint64_t gdn_b200_input_side_workspace_bytes(const int32_t* cu_seqlens,
+                                                          int32_t num_seqs, int32_t qk_heads,
+                                                          int32_t value_heads, int32_t hidden);
+GDN_B200_API int32_t gdn_b200_input_side(const void* x, const void* w_qkv, const void* w_z,
+                                         const void* w_a, const void* w_b, const void* conv_w,
+                                         void* conv_state, const int32_t* cu_seqlens,
+                                         int32_t num_seqs, int32_t qk_heads,
+                                         int32_t value_heads, int32_t hidden,
+                                         int32_t use_conv_state, void* q, void* k, void* v,
+                                         void* z, void* a, void* b, void* workspace,
+                                         uint64_t workspace_bytes, void* stream);
+
+/* The whole layer from x: input side, then gdn_b200_layer_forward's path
+ * (the reference's Submit with GDN_FORWARD_V1 on x, P:3083-3547). */
+GDN_B200_API uint64_t gdn_b200_layer_forward_x_workspace_bytes(const int32_t* cu_seqlens,
+                                                               int32_t num_seqs,
+                                                               int32_t qk_heads,
+                                                               int32_t value_heads,
+                                                               int32_t hidden);
+GDN_B200_API int32_t gdn_b200_layer_forward_x(const void* x, const void* w_qkv, const void* w_z,
+                                              const void* w_a, const void* w_b,
+                                              const void* conv_w, void* conv_state,
+                                              const float* A_log, const float* dt_bias,
+                                              const void* gamma, const void* w_out,
+                                              float* state, void* out,
+                                              const int32_t* cu_seqlens, int32_t num_seqs,
+                                              int32_t qk_heads, int32_t value_heads,
+                                              int32_t hidden, int32_t use_conv_state,
+                                              void* workspace, uint64_t workspace_bytes,
+                                              void* stream);
+
+/* ----------------------------------------------------------------------
  * Head-parallel output tail with the rank reduction fused in.
  *
  * With the value heads split over world_size GPUs of one node (rank r holds

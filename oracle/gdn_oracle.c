@@ -445,3 +445,45 @@ ORACLE_EXPORT int32_t gdn_oracle_threads(void) {
   return 1;
 #endif
 }
+
+/* -------------------------------------------------- input side of the layer -- */
+
+/* Depthwise causal conv1d over the projected qkv channels, width 4 (history
+ * 3), SiLU, and the conv-state update, per packed sequence: the reference's
+ * aclnnCausalConv1d call (P:3132-3179; weight input 5 [4, channels], state
+ * region gdn.conv bf16 [S, 3, channels], zero history when the submission has
+ * no context, P:3163-3171), with the activation of Qwen3-Next's
+ * causal_conv1d_fn(activation="silu"):
+ *   out[t][c] = bf16( silu( sum_{k=0..3} w[k][c] * x[t-3+k][c] ) ),
+ * rows before the sequence taken from its state (zero when use_state is 0).
+ * The sum is accumulated in float in tap order (w0 x0, then fmaf of taps 1,
+ * 2, 3) and silu(y) = y / (1 + exp(-y)).  Afterwards the state of each
+ * sequence holds the last three rows of [history; x]. */
+ORACLE_EXPORT void gdn_oracle_causal_conv1d(const uint16_t* x, const uint16_t* w,
+                                            uint16_t* state, const int32_t* cu, int32_t nseq,
+                                            int64_t channels, int32_t use_state,
+                                            uint16_t* out) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int32_t s = 0; s < nseq; ++s) {
+    for (int64_t c = 0; c < channels; ++c) {
+      float h[3];
+      for (int i = 0; i < 3; ++i)
+        h[i] = use_state ? bf16_to_f32(state[((int64_t)s * 3 + i) * channels + c]) : 0.0f;
+      const float w0 = bf16_to_f32(w[c]), w1 = bf16_to_f32(w[channels + c]);
+      const float w2 = bf16_to_f32(w[2 * channels + c]), w3 = bf16_to_f32(w[3 * channels + c]);
+      for (int64_t t = cu[s]; t < cu[s + 1]; ++t) {
+        const float xt = bf16_to_f32(x[t * channels + c]);
+        float acc = w0 * h[0];
+        acc = fmaf(w1, h[1], acc);
+        acc = fmaf(w2, h[2], acc);
+        acc = fmaf(w3, xt, acc);
+        out[t * channels + c] = f32_to_bf16(acc / (1.0f + expf(-acc)));
+        h[0] = h[1];
+        h[1] = h[2];
+        h[2] = xt;
+      }
+      for (int i = 0; i < 3; ++i)
+        state[((int64_t)s * 3 + i) * channels + c] = f32_to_bf16(h[i]);
+    }
+  }
+}

@@ -58,6 +58,7 @@ def lib():
                                        _u16p, _u16p, _f32p, _u16p, _i32p, i32, i32, i32, i32,
                                        i32, i32, ctypes.c_void_p, ctypes.c_void_p]
         L.gdn_oracle_threads.restype = i32
+        L.gdn_oracle_causal_conv1d.argtypes = [_u16p, _u16p, _u16p, _i32p, i32, i64, i32, _u16p]
         _lib = L
     return _lib
 
@@ -163,3 +164,37 @@ def layer(q, k, v, a, b, z, A_log, dt_bias, gamma, w, state, cu_seqlens, mode=0,
     if want_o or want_gated:
         return out, o, gated
     return out
+
+
+# ------------------------------------------------------------ input side --
+
+def causal_conv1d(x, w, state, cu_seqlens, use_state=True):
+    """Depthwise causal conv (width 4) + SiLU over packed sequences.  x bf16
+    [T, C]; w bf16 [4, C]; state bf16 [S, 3, C] (updated in place).  Returns
+    bf16 [T, C]."""
+    T, C = x.shape
+    out = np.empty((T, C), np.uint16)
+    cu = np.ascontiguousarray(cu_seqlens, np.int32)
+    assert state.flags["C_CONTIGUOUS"] and state.dtype == np.uint16
+    lib().gdn_oracle_causal_conv1d(np.ascontiguousarray(x), np.ascontiguousarray(w), state, cu,
+                                   len(cu) - 1, C, 1 if use_state else 0, out)
+    return out
+
+
+def input_side(x, w_qkv, w_z, w_a, w_b, conv_w, conv_state, cu_seqlens, hk, hv, d=128,
+               use_state=True):
+    """Projections (qkv, z, a, b: x @ W^T, the reference's four aclnnMatmul
+    calls, P:3101-3130), causal conv + SiLU over qkv with the conv-state update
+    (P:3132-3179), and the q/k/v split (channels [0, hk d), [hk d, 2 hk d),
+    [2 hk d, 2 hk d + hv d); P:3186-3247).  ``conv_state`` is updated in
+    place.  Returns q, k, v, z (bf16 [T, heads, d]) and a, b (bf16 [T, hv])."""
+    T = x.shape[0]
+    qkv = gemm_bf16(x, w_qkv)
+    z = gemm_bf16(x, w_z)
+    a = gemm_bf16(x, w_a)
+    b = gemm_bf16(x, w_b)
+    conv = causal_conv1d(qkv, conv_w, conv_state, cu_seqlens, use_state)
+    q = np.ascontiguousarray(conv[:, :hk * d]).reshape(T, hk, d)
+    k = np.ascontiguousarray(conv[:, hk * d:2 * hk * d]).reshape(T, hk, d)
+    v = np.ascontiguousarray(conv[:, 2 * hk * d:]).reshape(T, hv, d)
+    return q, k, v, z.reshape(T, hv, d), a, b

@@ -352,6 +352,63 @@ static bool all_single_token(const gdn::ChunkTable& tab) {
   return true;
 }
 
+// Post-projection layer on validated arguments: core (decode kernel when
+// every sequence has one token, chunk kernels otherwise), then the tail.
+// `ws` is the workspace after its error word.
+static int32_t layer_forward_impl(const gdn::ChunkTable& tab, const void* q, const void* k,
+                                  const void* v, const void* a, const void* b, const void* z,
+                                  const float* A_log, const float* dt_bias, const void* gamma,
+                                  const void* w_out, float* state, void* out, int32_t qk_heads,
+                                  int32_t value_heads, int32_t hidden, uint8_t* ws, uint32_t* err,
+                                  cudaStream_t s) {
+  const int64_t T = tab.cu[tab.num_seqs];
+  const int64_t K = static_cast<int64_t>(value_heads) * GDN_B200_HEAD_DIM;
+  uint64_t off = 0;
+  uint16_t* o = reinterpret_cast<uint16_t*>(ws + off);
+  off += round256(static_cast<uint64_t>(T) * K * 2);
+  uint16_t* gated = reinterpret_cast<uint16_t*>(ws + off);
+  off += round256(static_cast<uint64_t>(T) * K * 2);
+  const bool decode = all_single_token(tab);
+  uint8_t* records = ws + off;
+  if (!decode) off += round256(gdn::chunk_workspace_bytes(tab, qk_heads, value_heads));
+  float* gemm_ws = reinterpret_cast<float*>(ws + off);
+  if (T == 0) return ok();
+  cudaError_t e;
+  if (decode) {
+    e = gdn::launch_decode(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
+                           static_cast<const uint16_t*>(v), static_cast<const uint16_t*>(a),
+                           static_cast<const uint16_t*>(b), A_log, dt_bias, state, nullptr,
+                           static_cast<const uint16_t*>(z), static_cast<const uint16_t*>(gamma),
+                           gated, tab.num_seqs, qk_heads, value_heads, s);
+    if (e != cudaSuccess) return cuda_status(e, "decode launch");
+  } else {
+    const int32_t r = chunk_prefill_impl(tab, q, k, v, a, b, A_log, dt_bias, state, o, qk_heads,
+                                         value_heads, records, err, s);
+    if (r != STATECENTRIC_QWEN38_OK) return r;
+    e = gdn::launch_tail_prologue(o, static_cast<const uint16_t*>(z),
+                                  static_cast<const uint16_t*>(gamma), gated, T, value_heads,
+                                  1.0e-6f, s);
+    if (e != cudaSuccess) return cuda_status(e, "tail prologue launch");
+  }
+  e = gdn::launch_tail_gemm(gated, static_cast<const uint16_t*>(w_out),
+                            static_cast<uint16_t*>(out), gemm_ws, T, hidden, static_cast<int>(K),
+                            err, s);
+  return cuda_status(e, "tail GEMM launch");
+}
+
+static uint64_t layer_scratch_bytes(const gdn::ChunkTable& tab, int32_t qk_heads,
+                                    int32_t value_heads, int32_t hidden) {
+  const int64_t T = tab.cu[tab.num_seqs];
+  const int64_t K = static_cast<int64_t>(value_heads) * GDN_B200_HEAD_DIM;
+  uint64_t bytes = 0;
+  bytes += round256(static_cast<uint64_t>(T) * K * 2);  // o
+  bytes += round256(static_cast<uint64_t>(T) * K * 2);  // gated
+  if (!all_single_token(tab))
+    bytes += round256(gdn::chunk_workspace_bytes(tab, qk_heads, value_heads));
+  bytes += round256(gdn::tail_gemm_workspace_bytes(T, hidden, static_cast<int>(K)));
+  return bytes;
+}
+
 uint64_t gdn_b200_layer_forward_workspace_bytes(const int32_t* cu_seqlens, int32_t num_seqs,
                                                 int32_t qk_heads, int32_t value_heads,
                                                 int32_t hidden) {
@@ -359,15 +416,7 @@ uint64_t gdn_b200_layer_forward_workspace_bytes(const int32_t* cu_seqlens, int32
   if (!heads_ok(qk_heads, value_heads) || hidden <= 0 ||
       check_seqlens(cu_seqlens, num_seqs, &tab) != STATECENTRIC_QWEN38_OK)
     return 0;
-  const int64_t T = tab.cu[num_seqs];
-  const int64_t K = static_cast<int64_t>(value_heads) * GDN_B200_HEAD_DIM;
-  uint64_t bytes = kErrBytes;
-  bytes += round256(static_cast<uint64_t>(T) * K * 2);  // o
-  bytes += round256(static_cast<uint64_t>(T) * K * 2);  // gated
-  if (!all_single_token(tab))
-    bytes += round256(gdn::chunk_workspace_bytes(tab, qk_heads, value_heads));
-  bytes += round256(gdn::tail_gemm_workspace_bytes(T, hidden, static_cast<int>(K)));
-  return bytes;
+  return kErrBytes + layer_scratch_bytes(tab, qk_heads, value_heads, hidden);
 }
 
 int32_t gdn_b200_layer_forward(const void* q, const void* k, const void* v, const void* a,
@@ -398,44 +447,158 @@ int32_t gdn_b200_layer_forward(const void* q, const void* k, const void* v, cons
   if (workspace_bytes < need)
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT,
                 "workspace too small: need " + std::to_string(need) + " bytes");
-  const int64_t T = tab.cu[num_seqs];
-  const int64_t K = static_cast<int64_t>(value_heads) * GDN_B200_HEAD_DIM;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint32_t* err = reinterpret_cast<uint32_t*>(ws);
-  uint64_t off = kErrBytes;
-  uint16_t* o = reinterpret_cast<uint16_t*>(ws + off);
-  off += round256(static_cast<uint64_t>(T) * K * 2);
-  uint16_t* gated = reinterpret_cast<uint16_t*>(ws + off);
-  off += round256(static_cast<uint64_t>(T) * K * 2);
-  const bool decode = all_single_token(tab);
-  uint8_t* records = ws + off;
-  if (!decode) off += round256(gdn::chunk_workspace_bytes(tab, qk_heads, value_heads));
-  float* gemm_ws = reinterpret_cast<float*>(ws + off);
-
   cudaError_t e = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
   if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync");
-  if (T == 0) return ok();
-  if (decode) {
-    e = gdn::launch_decode(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
-                           static_cast<const uint16_t*>(v), static_cast<const uint16_t*>(a),
-                           static_cast<const uint16_t*>(b), A_log, dt_bias, state, nullptr,
-                           static_cast<const uint16_t*>(z), static_cast<const uint16_t*>(gamma),
-                           gated, num_seqs, qk_heads, value_heads, s);
-    if (e != cudaSuccess) return cuda_status(e, "decode launch");
-  } else {
-    const int32_t r = chunk_prefill_impl(tab, q, k, v, a, b, A_log, dt_bias, state, o, qk_heads,
-                                         value_heads, records, err, s);
-    if (r != STATECENTRIC_QWEN38_OK) return r;
-    e = gdn::launch_tail_prologue(o, static_cast<const uint16_t*>(z),
-                                  static_cast<const uint16_t*>(gamma), gated, T, value_heads,
-                                  1.0e-6f, s);
-    if (e != cudaSuccess) return cuda_status(e, "tail prologue launch");
-  }
-  e = gdn::launch_tail_gemm(gated, static_cast<const uint16_t*>(w_out),
-                            static_cast<uint16_t*>(out), gemm_ws, T, hidden, static_cast<int>(K),
-                            err, s);
-  return cuda_status(e, "tail GEMM launch");
+  return layer_forward_impl(tab, q, k, v, a, b, z, A_log, dt_bias, gamma, w_out, state, out,
+                            qk_heads, value_heads, hidden, ws + kErrBytes, err, s);
+}
+
+// ------------------------------------------------------- input side ----
+
+uint64_t gdn_b200_input_side_workspace_bytes(const int32_t* cu_seqlens, int32_t num_seqs,
+                                             int32_t qk_heads, int32_t value_heads,
+                                             int32_t hidden) {
+  gdn::ChunkTable tab;
+  if (!heads_ok(qk_heads, value_heads) || hidden <= 0 ||
+      check_seqlens(cu_seqlens, num_seqs, &tab) != STATECENTRIC_QWEN38_OK)
+    return 0;
+  return kErrBytes + round256(gdn::input_side_scratch_bytes(tab.cu[num_seqs], qk_heads,
+                                                            value_heads, hidden));
+}
+
+static int32_t check_input_side(const void* x, const void* w_qkv, const void* w_z,
+                                const void* w_a, const void* w_b, const void* conv_w,
+                                const void* conv_state, int32_t qk_heads, int32_t value_heads,
+                                int32_t hidden) {
+  if (!heads_ok(qk_heads, value_heads))
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT,
+                "value_heads must be a positive multiple of qk_heads");
+  if (hidden <= 0 || hidden % 128 != 0)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "hidden must be a positive multiple of 128");
+  if (x == nullptr || w_qkv == nullptr || w_z == nullptr || w_a == nullptr || w_b == nullptr ||
+      conv_w == nullptr || conv_state == nullptr)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
+  if (!aligned16(x) || !aligned16(w_qkv) || !aligned16(w_z) || !aligned16(w_a) ||
+      !aligned16(w_b) || !aligned16(conv_w) || !aligned16(conv_state))
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  return ok();
+}
+
+int32_t gdn_b200_input_side(const void* x, const void* w_qkv, const void* w_z, const void* w_a,
+                            const void* w_b, const void* conv_w, void* conv_state,
+                            const int32_t* cu_seqlens, int32_t num_seqs, int32_t qk_heads,
+                            int32_t value_heads, int32_t hidden, int32_t use_conv_state,
+                            void* q, void* k, void* v, void* z, void* a, void* b,
+                            void* workspace, uint64_t workspace_bytes, void* stream) {
+  int32_t st = check_input_side(x, w_qkv, w_z, w_a, w_b, conv_w, conv_state, qk_heads,
+                                value_heads, hidden);
+  if (st != STATECENTRIC_QWEN38_OK) return st;
+  gdn::ChunkTable tab;
+  st = check_seqlens(cu_seqlens, num_seqs, &tab);
+  if (st != STATECENTRIC_QWEN38_OK) return st;
+  if (q == nullptr || k == nullptr || v == nullptr || z == nullptr || a == nullptr ||
+      b == nullptr || workspace == nullptr)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(z) || !aligned16(workspace))
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  const uint64_t need = gdn_b200_input_side_workspace_bytes(cu_seqlens, num_seqs, qk_heads,
+                                                            value_heads, hidden);
+  if (workspace_bytes < need)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT,
+                "workspace too small: need " + std::to_string(need) + " bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws);
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync");
+  e = gdn::launch_input_side(
+      tab, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w_qkv),
+      static_cast<const uint16_t*>(w_z), static_cast<const uint16_t*>(w_a),
+      static_cast<const uint16_t*>(w_b), static_cast<const uint16_t*>(conv_w),
+      static_cast<uint16_t*>(conv_state), use_conv_state != 0, static_cast<uint16_t*>(q),
+      static_cast<uint16_t*>(k), static_cast<uint16_t*>(v), static_cast<uint16_t*>(z),
+      static_cast<uint16_t*>(a), static_cast<uint16_t*>(b), qk_heads, value_heads, hidden,
+      ws + kErrBytes, err, s);
+  return cuda_status(e, "input side launch");
+}
+
+// Layout after the error word: q, k, v, z, a, b, the input-side scratch, then
+// the post-projection layer's scratch.
+uint64_t gdn_b200_layer_forward_x_workspace_bytes(const int32_t* cu_seqlens, int32_t num_seqs,
+                                                  int32_t qk_heads, int32_t value_heads,
+                                                  int32_t hidden) {
+  gdn::ChunkTable tab;
+  if (!heads_ok(qk_heads, value_heads) || hidden <= 0 ||
+      check_seqlens(cu_seqlens, num_seqs, &tab) != STATECENTRIC_QWEN38_OK)
+    return 0;
+  const uint64_t T = static_cast<uint64_t>(tab.cu[num_seqs]);
+  const uint64_t qk = T * qk_heads * GDN_B200_HEAD_DIM * 2;
+  const uint64_t vv = T * value_heads * GDN_B200_HEAD_DIM * 2;
+  const uint64_t gate = T * value_heads * 2;
+  return kErrBytes + 2 * round256(qk) + 2 * round256(vv) + 2 * round256(gate) +
+         round256(gdn::input_side_scratch_bytes(T, qk_heads, value_heads, hidden)) +
+         layer_scratch_bytes(tab, qk_heads, value_heads, hidden);
+}
+
+int32_t gdn_b200_layer_forward_x(const void* x, const void* w_qkv, const void* w_z,
+                                 const void* w_a, const void* w_b, const void* conv_w,
+                                 void* conv_state, const float* A_log, const float* dt_bias,
+                                 const void* gamma, const void* w_out, float* state, void* out,
+                                 const int32_t* cu_seqlens, int32_t num_seqs, int32_t qk_heads,
+                                 int32_t value_heads, int32_t hidden, int32_t use_conv_state,
+                                 void* workspace, uint64_t workspace_bytes, void* stream) {
+  int32_t st = check_input_side(x, w_qkv, w_z, w_a, w_b, conv_w, conv_state, qk_heads,
+                                value_heads, hidden);
+  if (st != STATECENTRIC_QWEN38_OK) return st;
+  gdn::ChunkTable tab;
+  st = check_seqlens(cu_seqlens, num_seqs, &tab);
+  if (st != STATECENTRIC_QWEN38_OK) return st;
+  if (A_log == nullptr || dt_bias == nullptr || gamma == nullptr || w_out == nullptr ||
+      state == nullptr || out == nullptr || workspace == nullptr)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
+  if (!aligned16(gamma) || !aligned16(w_out) || !aligned16(state) || !aligned16(out) ||
+      !aligned16(workspace))
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  const uint64_t need = gdn_b200_layer_forward_x_workspace_bytes(cu_seqlens, num_seqs, qk_heads,
+                                                                 value_heads, hidden);
+  if (workspace_bytes < need)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT,
+                "workspace too small: need " + std::to_string(need) + " bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws);
+  const uint64_t T = static_cast<uint64_t>(tab.cu[num_seqs]);
+  const uint64_t qk = T * qk_heads * GDN_B200_HEAD_DIM * 2;
+  const uint64_t vv = T * value_heads * GDN_B200_HEAD_DIM * 2;
+  const uint64_t gate = T * value_heads * 2;
+  uint64_t off = kErrBytes;
+  auto take = [&](uint64_t bytes) {
+    uint16_t* p = reinterpret_cast<uint16_t*>(ws + off);
+    off += round256(bytes);
+    return p;
+  };
+  uint16_t* q = take(qk);
+  uint16_t* k = take(qk);
+  uint16_t* v = take(vv);
+  uint16_t* z = take(vv);
+  uint16_t* a = take(gate);
+  uint16_t* b = take(gate);
+  uint8_t* in_scratch = ws + off;
+  off += round256(gdn::input_side_scratch_bytes(T, qk_heads, value_heads, hidden));
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync");
+  e = gdn::launch_input_side(tab, static_cast<const uint16_t*>(x),
+                             static_cast<const uint16_t*>(w_qkv), static_cast<const uint16_t*>(w_z),
+                             static_cast<const uint16_t*>(w_a), static_cast<const uint16_t*>(w_b),
+                             static_cast<const uint16_t*>(conv_w),
+                             static_cast<uint16_t*>(conv_state), use_conv_state != 0, q, k, v, z,
+                             a, b, qk_heads, value_heads, hidden, in_scratch, err, s);
+  if (e != cudaSuccess) return cuda_status(e, "input side launch");
+  return layer_forward_impl(tab, q, k, v, a, b, z, A_log, dt_bias, gamma, w_out, state, out,
+                            qk_heads, value_heads, hidden, ws + off, err, s);
 }
 
 // -------------------------------------------------- synthetic inputs ----

@@ -36,6 +36,18 @@ cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uin
 cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out, float* ws,
                              int64_t M, int N, int K, uint32_t* err, cudaStream_t stream);
 
+// Input side: projections, causal conv + SiLU, q/k/v split, conv-state
+// update (gdn_input.cu).  a, b come from one GEMM over [w_a; w_b] padded to
+// input_gate_width(value_heads) rows.
+int input_gate_width(int value_heads);
+uint64_t input_side_scratch_bytes(int64_t tokens, int qk_heads, int value_heads, int hidden);
+cudaError_t launch_input_side(const ChunkTable& tab, const uint16_t* x, const uint16_t* w_qkv,
+                              const uint16_t* w_z, const uint16_t* w_a, const uint16_t* w_b,
+                              const uint16_t* conv_w, uint16_t* conv_state, int use_state,
+                              uint16_t* q, uint16_t* k, uint16_t* v, uint16_t* z, uint16_t* a,
+                              uint16_t* b, int qk_heads, int value_heads, int hidden,
+                              uint8_t* scratch, uint32_t* err, cudaStream_t stream);
+
 // Head-parallel tail with the rank reduction fused in (gdn_tail_allreduce.cu).
 constexpr int kTailMaxRanks = 8;
 constexpr int kTailArGrid = 148;  // CTAs per rank (same on every rank)

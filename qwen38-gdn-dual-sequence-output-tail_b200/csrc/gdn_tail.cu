@@ -500,7 +500,7 @@ TailGemmPlan plan_tail_gemm(int64_t M, int N, int K) {
     return p;
   }
   p.cluster = false;
-  p.bn = (N % 256 == 0) ? 256 : 128;
+  p.bn = (N % 256 == 0) ? 256 : (N % 128 == 0 ? 128 : 64);
   p.tiles_m = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
   p.tiles_n = N / p.bn;
   p.kblocks_total = K / kGemmBK;
@@ -580,8 +580,9 @@ cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out
     return cudaLaunchKernelEx(&cfg, tail_gemm_cluster_kernel<kClusterBN>, ta, tb, out, static_cast<int>(M), N,
                               p.kblocks_total, p.kblocks_per_split, err);
   }
-  cudaError_t e = (p.bn == 256) ? launch_gemm_bn<256>(ta, tb, out, ws, M, N, p, err, stream)
-                                : launch_gemm_bn<128>(ta, tb, out, ws, M, N, p, err, stream);
+  cudaError_t e = (p.bn == 256)   ? launch_gemm_bn<256>(ta, tb, out, ws, M, N, p, err, stream)
+                  : (p.bn == 128) ? launch_gemm_bn<128>(ta, tb, out, ws, M, N, p, err, stream)
+                                  : launch_gemm_bn<64>(ta, tb, out, ws, M, N, p, err, stream);
   if (e != cudaSuccess) return e;
   if (p.splits > 1) {
     const int64_t n4 = M * N / 4;

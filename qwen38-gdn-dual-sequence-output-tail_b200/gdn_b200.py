@@ -46,6 +46,10 @@ EXPORTED_SYMBOLS = (
     "gdn_b200_layer_forward_workspace_bytes",
     "gdn_b200_layer_forward",
     "gdn_b200_fill_synthetic",
+    "gdn_b200_input_side_workspace_bytes",
+    "gdn_b200_input_side",
+    "gdn_b200_layer_forward_x_workspace_bytes",
+    "gdn_b200_layer_forward_x",
     "gdn_b200_tail_exchange_bytes",
     "gdn_b200_exchange_alloc",
     "gdn_b200_exchange_free",
@@ -97,6 +101,14 @@ def lib() -> ctypes.CDLL:
         L.gdn_b200_layer_forward.restype = i32
         L.gdn_b200_fill_synthetic.argtypes = [u64, u64, u64, i32, f32, f32, i32, vp]
         L.gdn_b200_fill_synthetic.restype = i32
+        L.gdn_b200_input_side_workspace_bytes.argtypes = [i32p, i32, i32, i32, i32]
+        L.gdn_b200_input_side_workspace_bytes.restype = u64
+        L.gdn_b200_input_side.argtypes = [vp] * 7 + [i32p, i32, i32, i32, i32, i32] + [vp] * 7 + [u64, vp]
+        L.gdn_b200_input_side.restype = i32
+        L.gdn_b200_layer_forward_x_workspace_bytes.argtypes = [i32p, i32, i32, i32, i32]
+        L.gdn_b200_layer_forward_x_workspace_bytes.restype = u64
+        L.gdn_b200_layer_forward_x.argtypes = [vp] * 13 + [i32p, i32, i32, i32, i32, i32, vp, u64, vp]
+        L.gdn_b200_layer_forward_x.restype = i32
         L.gdn_b200_tail_exchange_bytes.argtypes = [i64, i32, i32]
         L.gdn_b200_tail_exchange_bytes.restype = u64
         L.gdn_b200_exchange_alloc.argtypes = [u64, ctypes.POINTER(vp)]
@@ -223,6 +235,70 @@ def layer_forward(q, k, v, a, b, z, A_log, dt_bias, gamma, w_out, state, cu_seql
                                         _ptr(A_log), _ptr(dt_bias), _ptr(gamma), _ptr(w_out),
                                         _ptr(state), _ptr(out), p, len(arr) - 1, hk, hv, hidden,
                                         _ptr(workspace), workspace.numel(), _stream(stream)))
+    return out
+
+
+# ------------------------------------------------------------ input side --
+
+def input_side_workspace_bytes(cu_seqlens, qk_heads: int, value_heads: int, hidden: int) -> int:
+    arr, p = _cu_array(cu_seqlens)
+    return int(lib().gdn_b200_input_side_workspace_bytes(p, len(arr) - 1, qk_heads, value_heads,
+                                                         hidden))
+
+
+def input_side(x, w_qkv, w_z, w_a, w_b, conv_w, conv_state, cu_seqlens, qk_heads: int,
+               use_conv_state=True, workspace=None, stream=None):
+    """x bf16 [T, hidden] -> (q, k, v, z, a, b) on the device; conv_state is
+    updated in place."""
+    import torch
+    T, hidden = x.shape
+    hv = w_z.shape[0] // HEAD_DIM
+    arr, p = _cu_array(cu_seqlens)
+    dev = x.device
+    q = torch.empty(T, qk_heads, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty(T, hv, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    z = torch.empty_like(v)
+    a = torch.empty(T, hv, dtype=torch.bfloat16, device=dev)
+    b = torch.empty_like(a)
+    if workspace is None:
+        workspace = _workspace(input_side_workspace_bytes(arr, qk_heads, hv, hidden), dev)
+    _check(lib().gdn_b200_input_side(_ptr(x), _ptr(w_qkv), _ptr(w_z), _ptr(w_a), _ptr(w_b),
+                                     _ptr(conv_w), _ptr(conv_state), p, len(arr) - 1, qk_heads,
+                                     hv, hidden, 1 if use_conv_state else 0, _ptr(q), _ptr(k),
+                                     _ptr(v), _ptr(z), _ptr(a), _ptr(b), _ptr(workspace),
+                                     workspace.numel(), _stream(stream)))
+    return q, k, v, z, a, b
+
+
+def layer_forward_x_workspace_bytes(cu_seqlens, qk_heads: int, value_heads: int,
+                                    hidden: int) -> int:
+    arr, p = _cu_array(cu_seqlens)
+    return int(lib().gdn_b200_layer_forward_x_workspace_bytes(p, len(arr) - 1, qk_heads,
+                                                              value_heads, hidden))
+
+
+def layer_forward_x(x, w_qkv, w_z, w_a, w_b, conv_w, conv_state, A_log, dt_bias, gamma, w_out,
+                    state, cu_seqlens, qk_heads: int, use_conv_state=True, out=None,
+                    workspace=None, stream=None):
+    """The whole layer from x; conv_state and state are updated in place.
+    The projections' input width and the output width are both ``hidden``."""
+    import torch
+    T, hidden = x.shape
+    if w_out.shape[0] != hidden:
+        raise GdnError(INVALID_ARGUMENT, "w_out rows must equal the hidden size of x")
+    hv = w_z.shape[0] // HEAD_DIM
+    arr, p = _cu_array(cu_seqlens)
+    if out is None:
+        out = torch.empty(T, w_out.shape[0], dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        workspace = _workspace(layer_forward_x_workspace_bytes(arr, qk_heads, hv, hidden),
+                               x.device)
+    _check(lib().gdn_b200_layer_forward_x(
+        _ptr(x), _ptr(w_qkv), _ptr(w_z), _ptr(w_a), _ptr(w_b), _ptr(conv_w), _ptr(conv_state),
+        _ptr(A_log), _ptr(dt_bias), _ptr(gamma), _ptr(w_out), _ptr(state), _ptr(out), p,
+        len(arr) - 1, qk_heads, hv, hidden,
+        1 if use_conv_state else 0, _ptr(workspace), workspace.numel(), _stream(stream)))
     return out
 
 
@@ -370,7 +446,8 @@ class Geometry:
 
 
 # Tensor ids of the seeded generator.
-TID = dict(q=1, k=2, v=3, a=4, b=5, z=6, A_log=7, dt_bias=8, gamma=9, w_out=10, state=11, o=12)
+TID = dict(q=1, k=2, v=3, a=4, b=5, z=6, A_log=7, dt_bias=8, gamma=9, w_out=10, state=11, o=12,
+           x=13, w_qkv=14, w_z=15, w_a=16, w_b=17, conv_w=18, conv_state=19)
 
 
 def synthetic_layer_inputs(cu_seqlens, geom: Geometry, seed: int = 0, state_std: float = 0.0,
@@ -413,6 +490,32 @@ def synthetic_layer_inputs(cu_seqlens, geom: Geometry, seed: int = 0, state_std:
         x["dt_bias"] = np.ascontiguousarray(x["dt_bias"][vs])
         x["w_out"] = np.ascontiguousarray(x["w_out"][:, rank * hv_r * D:(rank + 1) * hv_r * D])
         x["state"] = np.ascontiguousarray(x["state"][:, vs])
+    return x
+
+
+def synthetic_input_side(cu_seqlens, geom: Geometry, seed: int = 0, conv_state_std: float = 0.0):
+    """Host inputs of the input side: x ~ N(0,1) [T, hidden]; w_qkv, w_z,
+    w_a, w_b ~ N(0, 0.02) [N, hidden] (so the projections are ~N(0, 0.9));
+    conv_w ~ N(0, 0.5) [4, channels]; conv_state ~ N(0, conv_state_std)
+    [S, 3, channels] bf16 (zero when the std is 0)."""
+    cu = np.asarray(cu_seqlens, dtype=np.int64)
+    T = int(cu[-1])
+    S = len(cu) - 1
+    hk, hv, H, D = geom.qk_heads, geom.value_heads, geom.hidden, HEAD_DIM
+    C = (2 * hk + hv) * D
+    x = dict(
+        x=fill(seed, TID["x"], (T, H), NORMAL, 0.0, 1.0, BF16),
+        w_qkv=fill(seed, TID["w_qkv"], (C, H), NORMAL, 0.0, 0.02, BF16),
+        w_z=fill(seed, TID["w_z"], (hv * D, H), NORMAL, 0.0, 0.02, BF16),
+        w_a=fill(seed, TID["w_a"], (hv, H), NORMAL, 0.0, 0.02, BF16),
+        w_b=fill(seed, TID["w_b"], (hv, H), NORMAL, 0.0, 0.02, BF16),
+        conv_w=fill(seed, TID["conv_w"], (4, C), NORMAL, 0.0, 0.5, BF16),
+    )
+    if conv_state_std > 0:
+        x["conv_state"] = fill(seed, TID["conv_state"], (S, 3, C), NORMAL, 0.0, conv_state_std,
+                               BF16)
+    else:
+        x["conv_state"] = np.zeros((S, 3, C), np.uint16)
     return x
 
 

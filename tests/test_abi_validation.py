@@ -278,3 +278,46 @@ def test_exchange_entry_points_without_gpu_fail_loudly():
     assert region.value is None
     assert tail_ar(_group()) == G.INTERNAL
     assert lib().gdn_b200_exchange_export(None, None) == G.INVALID_ARGUMENT
+
+
+# ------------------------------------------------------------ input side --
+
+def _input_side(x=FAKE, conv_state=FAKE, cu=(0, 64, 128), hk=16, hv=32, hidden=2048, ws=FAKE,
+                ws_bytes=1 << 40, q=FAKE):
+    arr, p = _cu(list(cu))
+    return lib().gdn_b200_input_side(x, FAKE, FAKE, FAKE, FAKE, FAKE, conv_state, p,
+                                     len(arr) - 1, hk, hv, hidden, 1, q, FAKE, FAKE, FAKE, FAKE,
+                                     FAKE, ws, ws_bytes, None)
+
+
+@pytest.mark.parametrize("kwargs,fragment", [
+    (dict(hidden=1000), "multiple of 128"),
+    (dict(hv=30), "multiple of qk_heads"),
+    (dict(x=None), "null"),
+    (dict(conv_state=None), "null"),
+    (dict(q=None), "null"),
+    (dict(x=ODD), "aligned"),
+    (dict(cu=(1, 5)), "cu_seqlens[0]"),
+    (dict(ws_bytes=100), "workspace too small"),
+])
+def test_input_side_rejects(kwargs, fragment):
+    assert _input_side(**kwargs) == G.INVALID_ARGUMENT
+    assert fragment in G.last_error()
+
+
+def test_layer_forward_x_rejects_and_sizes():
+    arr, p = _cu([0, 64, 128])
+    args = [FAKE] * 13
+    assert lib().gdn_b200_layer_forward_x(*args, p, 2, 16, 32, 2048, 1, FAKE, 100, None) == \
+        G.INVALID_ARGUMENT
+    assert "workspace too small" in G.last_error()
+    args[7] = None  # A_log
+    assert lib().gdn_b200_layer_forward_x(*args, p, 2, 16, 32, 2048, 1, FAKE, 1 << 40, None) == \
+        G.INVALID_ARGUMENT
+    assert "null" in G.last_error()
+    # the layer-from-x workspace holds the input side's buffers and scratch
+    # plus the post-projection layer's
+    cu = [0, 4096, 8192]
+    assert G.layer_forward_x_workspace_bytes(cu, 16, 32, 2048) > \
+        G.layer_forward_workspace_bytes(cu, 16, 32, 2048) + \
+        G.input_side_workspace_bytes(cu, 16, 32, 2048) - 256

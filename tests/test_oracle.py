@@ -144,3 +144,56 @@ def test_bf16_rounding_matches_torch():
     ours = O.f32_to_bf16(x)
     theirs = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     assert np.array_equal(ours, theirs)
+
+
+# ------------------------------------------------------------ input side --
+
+def test_causal_conv_matches_transformers_update():
+    """The conv oracle against transformers 5.5.0's torch_causal_conv1d_update
+    (models/qwen3_next/modeling_qwen3_next.py: state rows concatenated before
+    the tokens, depthwise conv of width 4, SiLU, state <- the last rows), per
+    sequence, with and without a carried state, for sequences shorter and
+    longer than the three-row history."""
+    import torch
+    from transformers.models.qwen3_next.modeling_qwen3_next import torch_causal_conv1d_update
+    rng = np.random.default_rng(5)
+    C = 96
+    cu = np.array([0, 1, 3, 40, 41], np.int32)
+    x = O.f32_to_bf16(rng.normal(0, 1, (int(cu[-1]), C)).astype(np.float32))
+    w = O.f32_to_bf16(rng.normal(0, 0.5, (4, C)).astype(np.float32))
+    st0 = O.f32_to_bf16(rng.normal(0, 1, (4, 3, C)).astype(np.float32))
+    wt = torch.from_numpy(O.bf16_to_f32(w).T.copy())
+    for use_state in (True, False):
+        st = st0.copy()
+        out = O.causal_conv1d(x, w, st, cu, use_state)
+        same = total = 0
+        for s in range(len(cu) - 1):
+            hs = torch.from_numpy(O.bf16_to_f32(x[cu[s]:cu[s + 1]]).T.copy())[None]
+            cs = (torch.from_numpy(O.bf16_to_f32(st0[s]).T.copy())[None] if use_state
+                  else torch.zeros(1, C, 3))
+            ref = O.f32_to_bf16(torch_causal_conv1d_update(hs, cs, wt)[0].T.contiguous().numpy())
+            got = out[cu[s]:cu[s + 1]]
+            g, r = O.bf16_to_f32(got), O.bf16_to_f32(ref)
+            ulp = np.spacing(np.abs(r).astype(np.float32)) * 65536.0
+            assert (np.abs(g - r) <= ulp).all(), f"sequence {s}: beyond one bf16 ulp"
+            same += int((got == ref).sum())
+            total += got.size
+            assert np.array_equal(st[s], O.f32_to_bf16(cs[0].T.contiguous().numpy())), \
+                f"sequence {s}: conv state differs"
+        assert same / total > 0.97
+
+
+def test_causal_conv_continuation_is_exact():
+    """Splitting a sequence and carrying the conv state gives the same bits."""
+    rng = np.random.default_rng(6)
+    C = 64
+    x = O.f32_to_bf16(rng.normal(0, 1, (50, C)).astype(np.float32))
+    w = O.f32_to_bf16(rng.normal(0, 0.5, (4, C)).astype(np.float32))
+    st = O.f32_to_bf16(rng.normal(0, 1, (1, 3, C)).astype(np.float32))
+    st_a = st.copy()
+    whole = O.causal_conv1d(x, w, st_a, np.array([0, 50], np.int32))
+    st_b = st.copy()
+    parts = [O.causal_conv1d(x[i:j], w, st_b, np.array([0, j - i], np.int32))
+             for i, j in ((0, 2), (2, 3), (3, 29), (29, 50))]
+    assert np.array_equal(whole, np.concatenate(parts))
+    assert np.array_equal(st_a, st_b)
