@@ -304,15 +304,32 @@ def main():
     else:
         tail_ms = timed(lambda: G.output_tail(o, t["z"], t["gamma"], t["w_out"], out=out,
                                               workspace=ws_tail, stream=stream), args.steps, 2)
+    # The input side (x -> projections -> causal conv + SiLU -> q/k/v split,
+    # conv-state update) on the same tokens, timed alone: the layer from x
+    # adds it in front of the path above.
+    xs = G.to_device(G.synthetic_input_side(cu, geom, seed=2 + 1000 * rank,
+                                            conv_state_std=1.0), dev)
+    ws_in = torch.empty(G.input_side_workspace_bytes(cu, hk, hv, HIDDEN), dtype=torch.uint8,
+                        device=dev)
+    in_out = (torch.empty_like(t["q"]), torch.empty_like(t["k"]), torch.empty_like(t["v"]),
+              torch.empty_like(t["z"]), torch.empty_like(t["a"]), torch.empty_like(t["b"]))
+    in_ms = timed(lambda: G.input_side(xs["x"], xs["w_qkv"], xs["w_z"], xs["w_a"], xs["w_b"],
+                                       xs["conv_w"], xs["conv_state"], cu, hk, out=in_out,
+                                       workspace=ws_in, stream=stream), args.steps, 2)
+    G.workspace_status(ws_in, stream)
     hbm_peak, tf_peak, peak_kind = load_peaks()
     chunks = nseq * (SEQ_LEN // 64)
     core_flop = CHUNK_MFLOP * 1e6 * chunks * hv
     tail_flop = 2.0 * T * (hv * 128) * HIDDEN
     core_tf = core_flop / (core_ms * 1e-3) / 1e12
     tail_tf = tail_flop / (tail_ms * 1e-3) / 1e12
+    in_flop = 2.0 * T * HIDDEN * ((2 * hk + hv) * 128 + hv * 128 + 2 * hv)
+    in_tf = in_flop / (in_ms * 1e-3) / 1e12
     comps = {
         "chunk_core": {"ms": core_ms, "tflops": core_tf, "frac": core_tf / tf_peak},
         "output_tail": {"ms": tail_ms, "tflops": tail_tf, "frac": tail_tf / tf_peak},
+        "input_side": {"ms": in_ms, "tflops": in_tf, "frac": in_tf / tf_peak,
+                       "note": "x -> q,k,v,z,a,b (projections + causal conv), not in the step"},
     }
     dom = "chunk_core" if core_ms >= tail_ms else "output_tail"
     # Measured DRAM traffic is quoted for the single-GPU workload only (the

@@ -16,13 +16,17 @@
 // CUDA event recorded after the last kernel of the submission.
 //
 // Executed paths (flags always include GDN_FORWARD_V1):
+//   GDN_FORWARD_V1 alone or with a split variant (PREFILL_SPLIT_V2/V3,
+//     STRIDED_QKV_V4, POST_CONV_PACK_V5; the variants only change how the
+//     reference splits q/k/v, P:3186-3247): the reference's x-based layer,
+//     inputs x, w_qkv, w_z, w_a, w_b, conv_w, A_log, dt_bias, gamma, w_out
+//     (P:2387-2410); mutable state gdn.conv then gdn.recurrent (P:2313-2314);
+//     zero conv history when context_tokens is 0 (P:3163-3173).
 //   GDN_POST_PROJECTION_V6: inputs q, k, v, a, b, z, A_log, dt_bias, gamma,
 //     w_out; mutable state gdn.conv (validated, untouched) and gdn.recurrent;
 //     one packed decode launch when every sequence has one token, one
 //     chunked-prefill launch otherwise, then the flattened output tail.
 //   GDN_OUTPUT_TAIL_V7: inputs o, z, gamma, w_out; only the output tail.
-// The reference's x-based variants (projections + causal conv upstream of
-// this path) answer UNSUPPORTED.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -306,20 +310,18 @@ int32_t Submit(statecentric_qwen38_provider_handle_v1* handle,
       flags == (STATECENTRIC_QWEN38_GDN_FORWARD_V1 | STATECENTRIC_QWEN38_GDN_PREFILL_SPLIT_V3) ||
       flags == (STATECENTRIC_QWEN38_GDN_FORWARD_V1 | STATECENTRIC_QWEN38_GDN_PREFILL_STRIDED_QKV_V4) ||
       flags == (STATECENTRIC_QWEN38_GDN_FORWARD_V1 | STATECENTRIC_QWEN38_GDN_PREFILL_POST_CONV_PACK_V5);
-  if (known_reference_flag) {
-    return Fail(STATECENTRIC_QWEN38_UNSUPPORTED,
-                "the x-based GDN submission (input projections, causal conv) is not part of "
-                "this provider; submit GDN_POST_PROJECTION_V6 with projected q/k/v/a/b/z",
-                out_error);
-  }
-  if (flags != kV6 && flags != kV7) {
+  if (!known_reference_flag && flags != kV6 && flags != kV7) {
     return Fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "invalid Qwen3.8 GDN submission flags",
                 out_error);
   }
+  const bool from_x = known_reference_flag;
   const bool tail_only = flags == kV7;
   if ((tail_only && (execution->input_count != 4 || execution->mutable_state_count != 0)) ||
-      (!tail_only && (execution->input_count != 10 || execution->mutable_state == nullptr ||
-                      (execution->mutable_state_count != 1 && execution->mutable_state_count != 2)))) {
+      (from_x && (execution->input_count != 10 || execution->mutable_state == nullptr ||
+                  execution->mutable_state_count != 2)) ||
+      (!tail_only && !from_x &&
+       (execution->input_count != 10 || execution->mutable_state == nullptr ||
+        (execution->mutable_state_count != 1 && execution->mutable_state_count != 2)))) {
     return Fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "invalid Qwen3.8 GDN submission counts",
                 out_error);
   }
@@ -382,7 +384,28 @@ int32_t Submit(statecentric_qwen38_provider_handle_v1* handle,
 
   bool tensors_valid;
   const auto& out = execution->outputs[0];
-  if (tail_only) {
+  const uint64_t qkv = handle->qkv;
+  if (from_x) {
+    const uint64_t S = v.states;
+    tensors_valid =
+        TensorGeometry(in[0], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {tokens, hidden}, {int64_t(hidden), 1}, 2) &&
+        TensorGeometry(in[1], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {hidden, qkv}, {1, int64_t(hidden)}, 2) &&
+        TensorGeometry(in[2], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {hidden, value}, {1, int64_t(hidden)}, 2) &&
+        TensorGeometry(in[3], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {hidden, hv}, {1, int64_t(hidden)}, 2) &&
+        TensorGeometry(in[4], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {hidden, hv}, {1, int64_t(hidden)}, 2) &&
+        TensorGeometry(in[5], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {4, qkv}, {int64_t(qkv), 1}, 2) &&
+        TensorGeometry(in[6], dev, STATECENTRIC_QWEN38_SCALAR_F32, {hv}, {1}, 4) &&
+        TensorGeometry(in[7], dev, STATECENTRIC_QWEN38_SCALAR_F32, {hv}, {1}, 4) &&
+        TensorGeometry(in[8], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {D}, {1}, 2) &&
+        TensorGeometry(in[9], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {value, hidden}, {1, int64_t(value)}, 2) &&
+        TensorGeometry(out, dev, STATECENTRIC_QWEN38_SCALAR_BF16, {tokens, hidden}, {int64_t(hidden), 1}, 2) &&
+        StateRegion(*conv, execution->layer_index, "gdn.conv") &&
+        TensorGeometry(conv->tensor, dev, STATECENTRIC_QWEN38_SCALAR_BF16, {S, 3, qkv},
+                       {int64_t(3 * qkv), int64_t(qkv), 1}, 2) &&
+        StateRegion(*recurrent, execution->layer_index, "gdn.recurrent") &&
+        TensorGeometry(recurrent->tensor, dev, STATECENTRIC_QWEN38_SCALAR_F32, {S, hv, D, D},
+                       {int64_t(hv * D * D), int64_t(D * D), int64_t(D), 1}, 4);
+  } else if (tail_only) {
     tensors_valid =
         TensorGeometry(in[0], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {tokens, value}, {int64_t(value), 1}, 2) &&
         TensorGeometry(in[1], dev, STATECENTRIC_QWEN38_SCALAR_BF16, {tokens, value}, {int64_t(value), 1}, 2) &&
@@ -436,12 +459,18 @@ int32_t Submit(statecentric_qwen38_provider_handle_v1* handle,
   }
 
   const int32_t nseq = static_cast<int32_t>(v.states);
-  uint64_t ws_bytes = tail_only
-      ? gdn_b200_output_tail_workspace_bytes(static_cast<int64_t>(tokens), static_cast<int32_t>(hv),
-                                             static_cast<int32_t>(hidden))
-      : gdn_b200_layer_forward_workspace_bytes(v.cu.data(), nseq, static_cast<int32_t>(hk),
-                                               static_cast<int32_t>(hv),
-                                               static_cast<int32_t>(hidden));
+  uint64_t ws_bytes =
+      tail_only ? gdn_b200_output_tail_workspace_bytes(static_cast<int64_t>(tokens),
+                                                       static_cast<int32_t>(hv),
+                                                       static_cast<int32_t>(hidden))
+      : from_x  ? gdn_b200_layer_forward_x_workspace_bytes(v.cu.data(), nseq,
+                                                           static_cast<int32_t>(hk),
+                                                           static_cast<int32_t>(hv),
+                                                           static_cast<int32_t>(hidden))
+                : gdn_b200_layer_forward_workspace_bytes(v.cu.data(), nseq,
+                                                         static_cast<int32_t>(hk),
+                                                         static_cast<int32_t>(hv),
+                                                         static_cast<int32_t>(hidden));
   void* ws = AcquireWorkspace(handle, event, ws_bytes);
   if (ws == nullptr) {
     event->complete = true;
@@ -451,7 +480,19 @@ int32_t Submit(statecentric_qwen38_provider_handle_v1* handle,
   event->workspace = ws;
   void* stream = reinterpret_cast<void*>(execution->stream);
   int32_t status;
-  if (tail_only) {
+  if (from_x) {
+    status = gdn_b200_layer_forward_x(
+        reinterpret_cast<const void*>(in[0].data), reinterpret_cast<const void*>(in[1].data),
+        reinterpret_cast<const void*>(in[2].data), reinterpret_cast<const void*>(in[3].data),
+        reinterpret_cast<const void*>(in[4].data), reinterpret_cast<const void*>(in[5].data),
+        reinterpret_cast<void*>(conv->tensor.data), reinterpret_cast<const float*>(in[6].data),
+        reinterpret_cast<const float*>(in[7].data), reinterpret_cast<const void*>(in[8].data),
+        reinterpret_cast<const void*>(in[9].data),
+        reinterpret_cast<float*>(recurrent->tensor.data), reinterpret_cast<void*>(out.data),
+        v.cu.data(), nseq, static_cast<int32_t>(hk), static_cast<int32_t>(hv),
+        static_cast<int32_t>(hidden), execution->context_tokens != 0 ? 1 : 0, ws, ws_bytes,
+        stream);
+  } else if (tail_only) {
     status = gdn_b200_output_tail(reinterpret_cast<const void*>(in[0].data),
                                   reinterpret_cast<const void*>(in[1].data),
                                   reinterpret_cast<const void*>(in[2].data),

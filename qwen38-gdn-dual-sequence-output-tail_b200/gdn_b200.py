@@ -247,20 +247,23 @@ def input_side_workspace_bytes(cu_seqlens, qk_heads: int, value_heads: int, hidd
 
 
 def input_side(x, w_qkv, w_z, w_a, w_b, conv_w, conv_state, cu_seqlens, qk_heads: int,
-               use_conv_state=True, workspace=None, stream=None):
-    """x bf16 [T, hidden] -> (q, k, v, z, a, b) on the device; conv_state is
-    updated in place."""
+               use_conv_state=True, out=None, workspace=None, stream=None):
+    """x bf16 [T, hidden] -> (q, k, v, z, a, b) on the device (into ``out``
+    when given); conv_state is updated in place."""
     import torch
     T, hidden = x.shape
     hv = w_z.shape[0] // HEAD_DIM
     arr, p = _cu_array(cu_seqlens)
     dev = x.device
-    q = torch.empty(T, qk_heads, HEAD_DIM, dtype=torch.bfloat16, device=dev)
-    k = torch.empty_like(q)
-    v = torch.empty(T, hv, HEAD_DIM, dtype=torch.bfloat16, device=dev)
-    z = torch.empty_like(v)
-    a = torch.empty(T, hv, dtype=torch.bfloat16, device=dev)
-    b = torch.empty_like(a)
+    if out is not None:
+        q, k, v, z, a, b = out
+    else:
+        q = torch.empty(T, qk_heads, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        k = torch.empty_like(q)
+        v = torch.empty(T, hv, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        z = torch.empty_like(v)
+        a = torch.empty(T, hv, dtype=torch.bfloat16, device=dev)
+        b = torch.empty_like(a)
     if workspace is None:
         workspace = _workspace(input_side_workspace_bytes(arr, qk_heads, hv, hidden), dev)
     _check(lib().gdn_b200_input_side(_ptr(x), _ptr(w_qkv), _ptr(w_z), _ptr(w_a), _ptr(w_b),
@@ -812,6 +815,42 @@ class Provider:
         ex = self._execution(GDN_FORWARD_V1 | GDN_POST_PROJECTION_V6, inputs,
                              tensor_view(out, device=dv), states, T,
                              _stream(stream).value or 0, batch)
+        return self.submit(ex, deadline_s)
+
+    def submit_layer_x(self, xs, t, conv_state, state, out, cu_seqlens, context_tokens=0,
+                       flags=None, stream=None, deadline_s=60.0):
+        """The reference's x-based GDN layer (GDN_FORWARD_V1, optionally with
+        a split-variant flag): ``xs`` holds x, w_qkv, w_z, w_a, w_b, conv_w and
+        ``t`` holds A_log, dt_bias, gamma, w_out as torch tensors; conv_state
+        and state are the gdn.conv / gdn.recurrent regions (updated in place).
+        ``context_tokens`` 0 means no earlier context: zero conv history."""
+        g = self.geom
+        T, H = xs["x"].shape
+        D = HEAD_DIM
+        dv = self.device
+        C = (2 * g.qk_heads + g.value_heads) * D
+        inputs = [
+            tensor_view(xs["x"], [T, H], [H, 1], dv),
+            tensor_view(xs["w_qkv"], [H, C], [1, H], dv),
+            tensor_view(xs["w_z"], [H, g.value], [1, H], dv),
+            tensor_view(xs["w_a"], [H, g.value_heads], [1, H], dv),
+            tensor_view(xs["w_b"], [H, g.value_heads], [1, H], dv),
+            tensor_view(xs["conv_w"], [4, C], [C, 1], dv),
+            tensor_view(t["A_log"], [g.value_heads], [1], dv),
+            tensor_view(t["dt_bias"], [g.value_heads], [1], dv),
+            tensor_view(t["gamma"], [D], [1], dv),
+            tensor_view(t["w_out"], [g.value, g.hidden], [1, g.value], dv),
+        ]
+        S = state.shape[0]
+        states = [StateRegionV1(_c.sizeof(StateRegionV1), ABI_V1, 0, 0, b"gdn.conv",
+                                tensor_view(conv_state, device=dv)),
+                  StateRegionV1(_c.sizeof(StateRegionV1), ABI_V1, 0, 0, b"gdn.recurrent",
+                                tensor_view(state, device=dv))]
+        batch = self.batch_metadata(cu_seqlens) if S > 1 else None
+        ex = self._execution(GDN_FORWARD_V1 if flags is None else flags, inputs,
+                             tensor_view(out, device=dv), states, T,
+                             _stream(stream).value or 0, batch)
+        ex.context_tokens = context_tokens
         return self.submit(ex, deadline_s)
 
     def submit_tail(self, o, z, gamma, w_out, out, stream=None, deadline_s=60.0):

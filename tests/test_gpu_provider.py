@@ -153,10 +153,11 @@ def test_reference_flags_and_layer_rules(setup, cuda):
     cu = [0, 64, 128]
     x, t = _inputs(cu, cuda)
     out = torch.empty(128, GEOM.hidden, dtype=torch.bfloat16, device=cuda)
+    # x-based flags need the x-based inputs and both state regions
     for flags in (G.GDN_FORWARD_V1, G.GDN_FORWARD_V1 | G.GDN_PREFILL_POST_CONV_PACK_V5,
                   G.GDN_FORWARD_V1 | G.GDN_PREFILL_SPLIT_V2):
-        _expect(G.UNSUPPORTED, lambda: _submit_raw(prov, t, t["state"], out, cu, stream,
-                                                   flags=flags), "not part of this provider")
+        _expect(G.INVALID_ARGUMENT, lambda: _submit_raw(prov, t, t["state"], out, cu, stream,
+                                                        flags=flags))
     _expect(G.INVALID_ARGUMENT, lambda: _submit_raw(prov, t, t["state"], out, cu, stream,
                                                     flags=G.GDN_POST_PROJECTION_V6))
     # Full-attention layers (layer_index % 4 == 3) are not GDN layers.
@@ -202,3 +203,35 @@ def test_pool_reuses_workspace_and_reports(cuda, capfd, monkeypatch):
     prov.close()
     err = capfd.readouterr().err
     assert '"allocations":1' in err and '"reuses":2' in err and '"drained":true' in err
+
+
+@pytest.mark.parametrize("flags_name,context", [("GDN_FORWARD_V1", 0),
+                                                ("GDN_PREFILL_POST_CONV_PACK_V5", 64),
+                                                ("GDN_PREFILL_SPLIT_V2", 0)])
+def test_provider_x_based_layer_matches_direct_entry_point(setup, cuda, flags_name, context):
+    """The reference's x-based submission runs the whole layer (projections,
+    causal conv with the gdn.conv state, core, tail) and gives the same bits
+    as gdn_b200_layer_forward_x; context_tokens 0 means zero conv history."""
+    import torch
+    prov, stream = setup
+    cu = [0, 100, 164]
+    xs = G.synthetic_input_side(cu, GEOM, seed=11, conv_state_std=1.0)
+    lx = G.synthetic_layer_inputs(cu, GEOM, seed=11, state_std=0.05)
+    tx = G.to_device(xs, cuda)
+    t = G.to_device({n: lx[n] for n in ("A_log", "dt_bias", "gamma", "w_out", "state")}, cuda)
+    flags = G.GDN_FORWARD_V1 | (0 if flags_name == "GDN_FORWARD_V1" else getattr(G, flags_name))
+    out_p = torch.empty(164, GEOM.hidden, dtype=torch.bfloat16, device=cuda)
+    cs_p, st_p = tx["conv_state"].clone(), t["state"].clone()
+    with torch.cuda.stream(stream):
+        ev = prov.submit_layer_x(tx, t, cs_p, st_p, out_p, cu, context_tokens=context,
+                                 flags=flags, stream=stream)
+    prov.wait(ev)
+    prov.release(ev)
+    cs_d, st_d = tx["conv_state"].clone(), t["state"].clone()
+    out_d = G.layer_forward_x(tx["x"], tx["w_qkv"], tx["w_z"], tx["w_a"], tx["w_b"],
+                              tx["conv_w"], cs_d, t["A_log"], t["dt_bias"], t["gamma"],
+                              t["w_out"], st_d, cu, GEOM.qk_heads, use_conv_state=context > 0)
+    torch.cuda.synchronize()
+    assert torch.equal(out_p, out_d)
+    assert torch.equal(st_p, st_d)
+    assert torch.equal(cs_p, cs_d)
