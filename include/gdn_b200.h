@@ -107,6 +107,34 @@ GDN_B200_API int32_t gdn_b200_decode_step(const void* q, const void* k, const vo
                              int32_t batch, int32_t qk_heads,
                              int32_t value_heads, void* stream);
 
+/* Decode with the state of sequence i at the device address state_rows[i]
+ * (a device array of `batch` uint64 addresses, each a 16-byte aligned f32
+ * [Hv, 128(v), 128(k)] row): slot binding, so the rows can live anywhere in a
+ * state pool.  A CUDA graph captured around this call is rebound to other
+ * slots by rewriting state_rows (the DIRECT binding of the reference's
+ * qwen38_gdn_graph_binding.h without the exact-address restriction).  The
+ * kernel trusts the addresses.  Otherwise as gdn_b200_decode_step. */
+GDN_B200_API int32_t gdn_b200_decode_step_rows(const void* q, const void* k, const void* v,
+                                               const void* a, const void* b,
+                                               const float* A_log, const float* dt_bias,
+                                               const uint64_t* state_rows, void* o_out,
+                                               const void* z, const void* gamma,
+                                               void* gated_out, int32_t batch,
+                                               int32_t qk_heads, int32_t value_heads,
+                                               void* stream);
+
+/* COPY graph binding (reference qwen38_gdn_graph_binding.h:27-73): gathers
+ * (gather != 0: state rows -> packed buffers) or scatters the conv and
+ * recurrent rows of `layout` with one cudaMemcpyAsync per row on `stream`,
+ * conv row first.  Every row is checked against the layout's arena before
+ * any copy is enqueued; a refused binding returns INVALID_ARGUMENT with the
+ * reference's reason and issues no copy.  packed_conv / packed_recurrent are
+ * device addresses of batch_size rows each. */
+GDN_B200_API int32_t gdn_b200_copy_graph_rows(
+    const statecentric_qwen38_gdn_layout_workspace_v1* layout, uint64_t batch_size,
+    uint64_t conv_bytes, uint64_t recurrent_bytes, uint64_t packed_conv,
+    uint64_t packed_recurrent, int32_t gather, void* stream);
+
 /* Chunked (C = 64) gated delta rule over packed variable-length sequences.
  * Replaces ChunkGdn (P:1641-1838) and the token-serial run_sequence
  * (P:3387-3469): every sequence length, any number of chunks, one call. */

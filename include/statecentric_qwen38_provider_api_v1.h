@@ -176,6 +176,30 @@ typedef struct statecentric_qwen38_gdn_batch_v1 {
   const uint32_t* token_counts;
 } statecentric_qwen38_gdn_batch_v1;
 
+/* Graph-slot binding of the GDN state rows (reference
+ * native/include/statecentric/qwen38_gdn_graph_binding.h:15-73, which uses
+ * every field below): where the conv and recurrent rows of a batch of at most
+ * four sequences live inside a state arena, and whether a captured graph
+ * embeds their addresses (DIRECT) or reaches them through private packed
+ * buffers that are gathered before and scattered after a replay (COPY).
+ * Field order and numeric values are not pinned by the reference. */
+#define STATECENTRIC_QWEN38_GDN_BINDING_COPY_V1 1u
+#define STATECENTRIC_QWEN38_GDN_BINDING_DIRECT_V1 2u
+#define STATECENTRIC_QWEN38_GDN_GRAPH_MAX_ROWS 4
+typedef struct statecentric_qwen38_gdn_layout_workspace_v1 {
+  uint32_t size;
+  uint32_t abi_version;
+  uint32_t batch_size;
+  uint32_t binding_mode;
+  uintptr_t arena;
+  uint64_t arena_bytes;
+  uint64_t required_arena_bytes;
+  uint64_t conv_bytes_per_row;
+  uint64_t recurrent_bytes_per_row;
+  uintptr_t conv_row_addresses[STATECENTRIC_QWEN38_GDN_GRAPH_MAX_ROWS];
+  uintptr_t recurrent_row_addresses[STATECENTRIC_QWEN38_GDN_GRAPH_MAX_ROWS];
+} statecentric_qwen38_gdn_layout_workspace_v1;
+
 /* Owned error (P:411-424). */
 typedef struct statecentric_qwen38_error_v1 {
   uint32_t size;

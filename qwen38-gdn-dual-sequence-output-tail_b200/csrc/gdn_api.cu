@@ -8,6 +8,7 @@
 
 #include "gdn_b200.h"
 #include "gdn_common.cuh"
+#include "gdn_graph_binding.h"
 #include "gdn_internal.h"
 
 namespace {
@@ -258,11 +259,13 @@ int32_t gdn_b200_output_tail_allreduce(const void* o, const void* z, const void*
 
 // ----------------------------------------------------------- decode ----
 
-int32_t gdn_b200_decode_step(const void* q, const void* k, const void* v, const void* a,
-                             const void* b, const float* A_log, const float* dt_bias,
-                             float* state, void* o_out, const void* z, const void* gamma,
-                             void* gated_out, int32_t batch, int32_t qk_heads,
-                             int32_t value_heads, void* stream) {
+// Decode on validated arguments: the state is either contiguous (`state`)
+// or addressed per sequence through the device table `state_rows`.
+static int32_t decode_impl(const void* q, const void* k, const void* v, const void* a,
+                           const void* b, const float* A_log, const float* dt_bias, float* state,
+                           const uint64_t* state_rows, void* o_out, const void* z,
+                           const void* gamma, void* gated_out, int32_t batch, int32_t qk_heads,
+                           int32_t value_heads, void* stream) {
   if (batch < 0 || batch > 65535)
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "batch must be in [0, 65535]");
   if (!heads_ok(qk_heads, value_heads))
@@ -270,11 +273,12 @@ int32_t gdn_b200_decode_step(const void* q, const void* k, const void* v, const 
                 "value_heads must be a positive multiple of qk_heads");
   if (batch == 0) return ok();
   if (q == nullptr || k == nullptr || v == nullptr || a == nullptr || b == nullptr ||
-      A_log == nullptr || dt_bias == nullptr || state == nullptr)
+      A_log == nullptr || dt_bias == nullptr || (state == nullptr && state_rows == nullptr))
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
   if ((gated_out != nullptr) && (z == nullptr || gamma == nullptr))
     return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "gated_out needs z and gamma");
-  if (!aligned16(state) || (reinterpret_cast<uintptr_t>(q) & 7u) || (reinterpret_cast<uintptr_t>(k) & 7u) ||
+  if ((state && !aligned16(state)) || (reinterpret_cast<uintptr_t>(state_rows) & 7u) ||
+      (reinterpret_cast<uintptr_t>(q) & 7u) || (reinterpret_cast<uintptr_t>(k) & 7u) ||
       (reinterpret_cast<uintptr_t>(v) & 7u) || (o_out && (reinterpret_cast<uintptr_t>(o_out) & 7u)) ||
       (gated_out && ((reinterpret_cast<uintptr_t>(gated_out) & 7u) || (reinterpret_cast<uintptr_t>(z) & 7u) ||
                      (reinterpret_cast<uintptr_t>(gamma) & 7u))))
@@ -285,8 +289,30 @@ int32_t gdn_b200_decode_step(const void* q, const void* k, const void* v, const 
       static_cast<const uint16_t*>(b), A_log, dt_bias, state, static_cast<uint16_t*>(o_out),
       static_cast<const uint16_t*>(z), static_cast<const uint16_t*>(gamma),
       static_cast<uint16_t*>(gated_out), batch, qk_heads, value_heads,
-      static_cast<cudaStream_t>(stream));
+      static_cast<cudaStream_t>(stream), state_rows);
   return cuda_status(e, "decode launch");
+}
+
+int32_t gdn_b200_decode_step(const void* q, const void* k, const void* v, const void* a,
+                             const void* b, const float* A_log, const float* dt_bias,
+                             float* state, void* o_out, const void* z, const void* gamma,
+                             void* gated_out, int32_t batch, int32_t qk_heads,
+                             int32_t value_heads, void* stream) {
+  if (batch > 0 && state == nullptr)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
+  return decode_impl(q, k, v, a, b, A_log, dt_bias, state, nullptr, o_out, z, gamma, gated_out,
+                     batch, qk_heads, value_heads, stream);
+}
+
+int32_t gdn_b200_decode_step_rows(const void* q, const void* k, const void* v, const void* a,
+                                  const void* b, const float* A_log, const float* dt_bias,
+                                  const uint64_t* state_rows, void* o_out, const void* z,
+                                  const void* gamma, void* gated_out, int32_t batch,
+                                  int32_t qk_heads, int32_t value_heads, void* stream) {
+  if (batch > 0 && state_rows == nullptr)
+    return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "null pointer argument");
+  return decode_impl(q, k, v, a, b, A_log, dt_bias, nullptr, state_rows, o_out, z, gamma,
+                     gated_out, batch, qk_heads, value_heads, stream);
 }
 
 // ------------------------------------------------------------ chunk ----
@@ -599,6 +625,27 @@ int32_t gdn_b200_layer_forward_x(const void* x, const void* w_qkv, const void* w
   if (e != cudaSuccess) return cuda_status(e, "input side launch");
   return layer_forward_impl(tab, q, k, v, a, b, z, A_log, dt_bias, gamma, w_out, state, out,
                             qk_heads, value_heads, hidden, ws + off, err, s);
+}
+
+// ---------------------------------------------------- graph binding ----
+
+int32_t gdn_b200_copy_graph_rows(const statecentric_qwen38_gdn_layout_workspace_v1* layout,
+                                 uint64_t batch_size, uint64_t conv_bytes,
+                                 uint64_t recurrent_bytes, uint64_t packed_conv,
+                                 uint64_t packed_recurrent, int32_t gather, void* stream) {
+  if (layout == nullptr) return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "layout is null");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t first = cudaSuccess;
+  const char* refused = gdn_b200::CopyGraphRows(
+      *layout, static_cast<std::size_t>(batch_size), conv_bytes, recurrent_bytes,
+      static_cast<uintptr_t>(packed_conv), static_cast<uintptr_t>(packed_recurrent), gather != 0,
+      [&](uintptr_t dst, uint64_t bytes, uintptr_t src) {
+        if (first == cudaSuccess)
+          first = cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src),
+                                  bytes, cudaMemcpyDeviceToDevice, s);
+      });
+  if (refused != nullptr) return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, refused);
+  return cuda_status(first, "cudaMemcpyAsync(graph rows)");
 }
 
 // -------------------------------------------------- synthetic inputs ----

@@ -47,7 +47,7 @@ gdn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k
                   const float* __restrict__ dt_bias, float* __restrict__ state,
                   uint16_t* __restrict__ o_out, const uint16_t* __restrict__ z,
                   const uint16_t* __restrict__ gamma, uint16_t* __restrict__ gated_out,
-                  int qk_heads, int value_heads) {
+                  const uint64_t* __restrict__ state_rows, int qk_heads, int value_heads) {
   const int h = blockIdx.x;
   const int seq = blockIdx.y;
   const int warp = threadIdx.x >> 5;
@@ -62,7 +62,13 @@ gdn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k
 
   const int64_t qk_row = (static_cast<int64_t>(seq) * qk_heads + kh) * kHeadDim;
   const int64_t v_row = (static_cast<int64_t>(seq) * value_heads + h) * kHeadDim;
-  float* srow0 = state + (static_cast<int64_t>(seq) * value_heads + h) * kHeadDim * kHeadDim;
+  // The sequence's state: row `seq` of the contiguous [S, Hv, 128, 128]
+  // state, or the [Hv, 128, 128] row at the address given for it (slot
+  // binding: the rows can sit anywhere in a state pool).
+  float* srow0 = (state_rows != nullptr
+                      ? reinterpret_cast<float*>(state_rows[seq])
+                      : state + static_cast<int64_t>(seq) * value_heads * kHeadDim * kHeadDim) +
+                 static_cast<int64_t>(h) * kHeadDim * kHeadDim;
 
   // Issue the state loads first: they are the long-latency stream.
   float4 s[kDecodeRowsPerWarp];
@@ -151,11 +157,12 @@ cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* 
                           const uint16_t* a, const uint16_t* b, const float* A_log,
                           const float* dt_bias, float* state, uint16_t* o_out,
                           const uint16_t* z, const uint16_t* gamma, uint16_t* gated_out,
-                          int batch, int qk_heads, int value_heads, cudaStream_t stream) {
+                          int batch, int qk_heads, int value_heads, cudaStream_t stream,
+                          const uint64_t* state_rows) {
   dim3 grid(value_heads, batch);
   gdn_decode_kernel<<<grid, kDecodeThreads, 0, stream>>>(q, k, v, a, b, A_log, dt_bias, state,
-                                                         o_out, z, gamma, gated_out, qk_heads,
-                                                         value_heads);
+                                                         o_out, z, gamma, gated_out, state_rows,
+                                                         qk_heads, value_heads);
   return cudaGetLastError();
 }
 

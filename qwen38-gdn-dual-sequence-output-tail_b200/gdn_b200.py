@@ -46,6 +46,8 @@ EXPORTED_SYMBOLS = (
     "gdn_b200_layer_forward_workspace_bytes",
     "gdn_b200_layer_forward",
     "gdn_b200_fill_synthetic",
+    "gdn_b200_decode_step_rows",
+    "gdn_b200_copy_graph_rows",
     "gdn_b200_input_side_workspace_bytes",
     "gdn_b200_input_side",
     "gdn_b200_layer_forward_x_workspace_bytes",
@@ -101,6 +103,11 @@ def lib() -> ctypes.CDLL:
         L.gdn_b200_layer_forward.restype = i32
         L.gdn_b200_fill_synthetic.argtypes = [u64, u64, u64, i32, f32, f32, i32, vp]
         L.gdn_b200_fill_synthetic.restype = i32
+        L.gdn_b200_decode_step_rows.argtypes = [vp] * 12 + [i32, i32, i32, vp]
+        L.gdn_b200_decode_step_rows.restype = i32
+        L.gdn_b200_copy_graph_rows.argtypes = [ctypes.POINTER(LayoutWorkspaceV1), u64, u64, u64,
+                                               u64, u64, i32, vp]
+        L.gdn_b200_copy_graph_rows.restype = i32
         L.gdn_b200_input_side_workspace_bytes.argtypes = [i32p, i32, i32, i32, i32]
         L.gdn_b200_input_side_workspace_bytes.restype = u64
         L.gdn_b200_input_side.argtypes = [vp] * 7 + [i32p, i32, i32, i32, i32, i32] + [vp] * 7 + [u64, vp]
@@ -236,6 +243,42 @@ def layer_forward(q, k, v, a, b, z, A_log, dt_bias, gamma, w_out, state, cu_seql
                                         _ptr(state), _ptr(out), p, len(arr) - 1, hk, hv, hidden,
                                         _ptr(workspace), workspace.numel(), _stream(stream)))
     return out
+
+
+# ------------------------------------------------------ graph binding --
+
+def decode_step_rows(q, k, v, a, b, A_log, dt_bias, state_rows, o_out=None, z=None, gamma=None,
+                     gated_out=None, stream=None):
+    """Decode with sequence i's state at the device address state_rows[i]
+    (``state_rows``: int64 tensor on the device)."""
+    batch, hk = q.shape[0], q.shape[1]
+    hv = v.shape[1]
+    _check(lib().gdn_b200_decode_step_rows(_ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b),
+                                           _ptr(A_log), _ptr(dt_bias), _ptr(state_rows),
+                                           _ptr(o_out), _ptr(z), _ptr(gamma), _ptr(gated_out),
+                                           batch, hk, hv, _stream(stream)))
+
+
+BINDING_COPY_V1, BINDING_DIRECT_V1, GRAPH_MAX_ROWS = 1, 2, 4
+
+
+class LayoutWorkspaceV1(ctypes.Structure):
+    """statecentric_qwen38_gdn_layout_workspace_v1 of the provider header."""
+    _fields_ = [("size", ctypes.c_uint32), ("abi_version", ctypes.c_uint32),
+                ("batch_size", ctypes.c_uint32), ("binding_mode", ctypes.c_uint32),
+                ("arena", ctypes.c_size_t), ("arena_bytes", ctypes.c_uint64),
+                ("required_arena_bytes", ctypes.c_uint64),
+                ("conv_bytes_per_row", ctypes.c_uint64),
+                ("recurrent_bytes_per_row", ctypes.c_uint64),
+                ("conv_row_addresses", ctypes.c_size_t * GRAPH_MAX_ROWS),
+                ("recurrent_row_addresses", ctypes.c_size_t * GRAPH_MAX_ROWS)]
+
+
+def copy_graph_rows(layout, batch_size, conv_bytes, recurrent_bytes, packed_conv,
+                    packed_recurrent, gather, stream=None):
+    _check(lib().gdn_b200_copy_graph_rows(ctypes.byref(layout), batch_size, conv_bytes,
+                                          recurrent_bytes, packed_conv, packed_recurrent,
+                                          1 if gather else 0, _stream(stream)))
 
 
 # ------------------------------------------------------------ input side --

@@ -30,6 +30,10 @@ int main(void) {
   F(statecentric_qwen38_provider_descriptor_v1, reserved2);
   S(gdn_b200_tail_group_v1); F(gdn_b200_tail_group_v1, max_rows);
   F(gdn_b200_tail_group_v1, hidden); F(gdn_b200_tail_group_v1, region);
+  S(statecentric_qwen38_gdn_layout_workspace_v1);
+  F(statecentric_qwen38_gdn_layout_workspace_v1, arena);
+  F(statecentric_qwen38_gdn_layout_workspace_v1, recurrent_bytes_per_row);
+  F(statecentric_qwen38_gdn_layout_workspace_v1, recurrent_row_addresses);
   printf("MIN_SIZE %zu\n", (size_t)STATECENTRIC_QWEN38_PROVIDER_DESCRIPTOR_V1_MIN_SIZE);
   return 0;
 }

@@ -55,6 +55,7 @@ def test_provider_abi_layout_matches_python_mirror(tmp_path):
         "statecentric_qwen38_completion_v1": G.CompletionV1,
         "statecentric_qwen38_provider_descriptor_v1": G.DescriptorV1,
         "gdn_b200_tail_group_v1": G.TailGroupV1,
+        "statecentric_qwen38_gdn_layout_workspace_v1": G.LayoutWorkspaceV1,
     }
     for key, value in c_layout.items():
         if key == "MIN_SIZE":
@@ -81,3 +82,8 @@ def test_library_exports_every_declared_symbol():
     assert declared <= exported, declared - exported
     for name in declared:
         getattr(G.lib(), name)
+
+
+def test_graph_binding_rules(tmp_path):
+    r = _build_and_run(tmp_path, "graph_binding_test.cpp")
+    assert r.returncode == 0, f"graph binding test failed with code {r.returncode}"
