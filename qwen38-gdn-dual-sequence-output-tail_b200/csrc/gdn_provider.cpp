@@ -61,6 +61,18 @@ struct statecentric_qwen38_provider_handle_v1 {
   std::unique_ptr<statecentric::CompletedBufferPool> pool;
   std::atomic<uint64_t> submissions{0};
   std::atomic<uint64_t> private_allocations{0};
+  // Admission telemetry (the reference's first-admission lines, P:590-723,
+  // for the paths that exist here): every validated GDN submission is a
+  // submit call; each executed path counts its admissions and writes one
+  // line to stderr at its first.
+  std::atomic<uint64_t> gdn_submit_calls{0};
+  std::atomic<uint64_t> packed_decode_admitted{0};
+  std::atomic<uint64_t> chunk_prefill_admitted{0};
+  std::atomic<uint64_t> input_side_admitted{0};
+  std::atomic<bool> packed_decode_emitted{false};
+  std::atomic<bool> decode_flat_output_emitted{false};
+  std::atomic<bool> chunk_prefill_emitted{false};
+  std::atomic<bool> input_side_emitted{false};
 };
 
 struct statecentric_qwen38_event_v1 {
@@ -77,6 +89,52 @@ struct statecentric_qwen38_event_v1 {
 namespace {
 
 constexpr uint32_t kAbi = STATECENTRIC_QWEN38_PROVIDER_ABI_V1;
+
+// One telemetry line, written once per handle (`flag` guards it).
+void EmitOnce(std::atomic<bool>& flag, const char* line) {
+  bool expected = false;
+  if (flag.compare_exchange_strong(expected, true, std::memory_order_acq_rel,
+                                   std::memory_order_relaxed)) {
+    std::fputs(line, stderr);
+    std::fflush(stderr);
+  }
+}
+
+void RecordAdmission(statecentric_qwen38_provider_handle_v1* h, bool from_x, bool decode,
+                     uint64_t sequences, uint64_t rows, uint64_t chunks) {
+  const auto submits = static_cast<unsigned long long>(h->gdn_submit_calls.load());
+  char line[320];
+  if (from_x) {
+    const auto n = static_cast<unsigned long long>(h->input_side_admitted.fetch_add(1) + 1);
+    std::snprintf(line, sizeof line,
+                  "STATECENTRIC_QWEN38_GDN_B200_INPUT_SIDE_TELEMETRY_V1="
+                  "{\"rank\":%u,\"submit_calls\":%llu,\"admitted_calls\":%llu}\n",
+                  h->rank, submits, n);
+    EmitOnce(h->input_side_emitted, line);
+  }
+  if (decode) {
+    const auto n = static_cast<unsigned long long>(h->packed_decode_admitted.fetch_add(1) + 1);
+    std::snprintf(line, sizeof line,
+                  "STATECENTRIC_QWEN38_GDN_PACKED_DECODE_TELEMETRY_V12="
+                  "{\"rank\":%u,\"submit_calls\":%llu,\"admitted_calls\":%llu}\n",
+                  h->rank, submits, n);
+    EmitOnce(h->packed_decode_emitted, line);
+    std::snprintf(line, sizeof line,
+                  "STATECENTRIC_QWEN38_GDN_DECODE_FLAT_OUTPUT_PROJECTION_V18="
+                  "{\"rank\":%u,\"admitted_calls\":%llu,\"rows\":%llu}\n",
+                  h->rank, n, static_cast<unsigned long long>(rows));
+    EmitOnce(h->decode_flat_output_emitted, line);
+  } else {
+    const auto n = static_cast<unsigned long long>(h->chunk_prefill_admitted.fetch_add(1) + 1);
+    std::snprintf(line, sizeof line,
+                  "STATECENTRIC_QWEN38_GDN_B200_CHUNK_PREFILL_TELEMETRY_V1="
+                  "{\"rank\":%u,\"submit_calls\":%llu,\"admitted_calls\":%llu,"
+                  "\"sequences\":%llu,\"chunks\":%llu}\n",
+                  h->rank, submits, n, static_cast<unsigned long long>(sequences),
+                  static_cast<unsigned long long>(chunks));
+    EmitOnce(h->chunk_prefill_emitted, line);
+  }
+}
 constexpr uint32_t kHeadDim = GDN_B200_HEAD_DIM;
 constexpr uint64_t kMaxTokensLimit = 1ull << 22;
 
@@ -376,6 +434,7 @@ int32_t Submit(statecentric_qwen38_provider_handle_v1* handle,
     v.cu = {0, static_cast<int32_t>(tokens)};
     v.counts = {static_cast<uint32_t>(tokens)};
   }
+  if (!tail_only) handle->gdn_submit_calls.fetch_add(1, std::memory_order_relaxed);
   const auto plan = statecentric::PlanGdnB200Submission(v.counts, handle->max_tokens,
                                                         GDN_B200_MAX_SEQUENCES);
   if (!plan.admitted)
@@ -521,6 +580,9 @@ int32_t Submit(statecentric_qwen38_provider_handle_v1* handle,
     return Fail(STATECENTRIC_QWEN38_INTERNAL, msg, out_error);
   }
   handle->submissions.fetch_add(1, std::memory_order_relaxed);
+  if (!tail_only)
+    RecordAdmission(handle, from_x, plan.core == statecentric::GdnB200Core::kPackedDecode,
+                    plan.sequences, plan.rows, plan.chunks);
   *out_event = event;
   return STATECENTRIC_QWEN38_OK;
 }

@@ -235,3 +235,37 @@ def test_provider_x_based_layer_matches_direct_entry_point(setup, cuda, flags_na
     assert torch.equal(out_p, out_d)
     assert torch.equal(st_p, st_d)
     assert torch.equal(cs_p, cs_d)
+
+
+def test_first_admission_telemetry(cuda, capfd):
+    """One line per executed path at its first admission (the reference's
+    first-admission telemetry, P:590-723): packed decode (V12) and its flat
+    output projection (V18) in the reference's format, and the B200 chunked
+    prefill path."""
+    import torch
+    stream = torch.cuda.Stream()
+    prov = G.Provider(GEOM, max_tokens=4096)
+    dec = [0, 1, 2, 3, 4]
+    _, td = _inputs(dec, cuda)
+    out_d = torch.empty(4, GEOM.hidden, dtype=torch.bfloat16, device=cuda)
+    for _ in range(2):
+        ev = prov.submit_layer(td, td["state"], out_d, dec, stream=stream)
+        prov.wait(ev)
+        prov.release(ev)
+    pre = [0, 64, 128]
+    _, tp = _inputs(pre, cuda)
+    out_p = torch.empty(128, GEOM.hidden, dtype=torch.bfloat16, device=cuda)
+    ev = prov.submit_layer(tp, tp["state"], out_p, pre, stream=stream)
+    prov.wait(ev)
+    prov.release(ev)
+    prov.close()
+    err = capfd.readouterr().err.splitlines()
+    decode = [l for l in err if l.startswith("STATECENTRIC_QWEN38_GDN_PACKED_DECODE_TELEMETRY_V12=")]
+    flat = [l for l in err if l.startswith("STATECENTRIC_QWEN38_GDN_DECODE_FLAT_OUTPUT_PROJECTION_V18=")]
+    chunk = [l for l in err if l.startswith("STATECENTRIC_QWEN38_GDN_B200_CHUNK_PREFILL_TELEMETRY_V1=")]
+    assert decode == ['STATECENTRIC_QWEN38_GDN_PACKED_DECODE_TELEMETRY_V12='
+                      '{"rank":0,"submit_calls":1,"admitted_calls":1}']
+    assert flat == ['STATECENTRIC_QWEN38_GDN_DECODE_FLAT_OUTPUT_PROJECTION_V18='
+                    '{"rank":0,"admitted_calls":1,"rows":4}']
+    assert chunk == ['STATECENTRIC_QWEN38_GDN_B200_CHUNK_PREFILL_TELEMETRY_V1='
+                     '{"rank":0,"submit_calls":3,"admitted_calls":1,"sequences":2,"chunks":2}']
