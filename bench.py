@@ -167,6 +167,95 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_secondary(args):
+    """The other measured shapes of the benchmark, one GPU, one JSON line:
+    ``decode``: one decode step of B=64 sequences (f32 state [64, 32, 128,
+    128] ~ N(0, 0.05), resident; the state read and written is the HBM
+    stream) plus the flattened tail over the 64 rows; ``tail``: the
+    dual-sequence output tail over 2 x 64 rows (o, z [128, 32, 128], w_out
+    [2048, 4096]; the weight read is the HBM stream).  Each timed step is one
+    call, with a 256 MB buffer written between steps so that every step
+    starts with the state / weight out of L2."""
+    import numpy as np
+    import torch
+    import gdn_b200 as G
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    geom = G.Geometry(QK_HEADS, V_HEADS, HIDDEN)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    if args.workload == "decode":
+        B = 64
+        cu = np.arange(B + 1, dtype=np.int32)
+        t = G.to_device(G.synthetic_layer_inputs(cu, geom, seed=5, state_std=0.05), dev)
+        out = torch.empty(B, HIDDEN, dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(G.layer_forward_workspace_bytes(cu, QK_HEADS, V_HEADS, HIDDEN),
+                         dtype=torch.uint8, device=dev)
+        fn = lambda: G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
+                                     t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu,
+                                     out=out, workspace=ws, stream=stream)
+        # the decode kernel alone (state read + write: the roofline stream)
+        gated = torch.empty(B, V_HEADS * 128, dtype=torch.bfloat16, device=dev)
+        kern = lambda: G.decode_step(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"],
+                                     t["dt_bias"], t["state"], z=t["z"], gamma=t["gamma"],
+                                     gated_out=gated, stream=stream)
+        kbytes = 2 * B * V_HEADS * 128 * 128 * 4
+        units, metric, kname = B, "GDN decode tokens/sec (B=64, one step + tail)", "gdn_decode_kernel"
+        desc = "decode step, 64 sequences x 1 token, Hk=16 Hv=32 D=128 hidden=2048"
+    else:
+        rows = 128
+        x = {n: G.fill(0, i, sh, G.NORMAL, mu, sd, G.BF16) for n, i, sh, mu, sd in (
+            ("o", 21, (rows, V_HEADS, 128), 0.0, 1.0), ("z", 22, (rows, V_HEADS, 128), 0.0, 1.0),
+            ("gamma", 23, (128,), 1.0, 0.02), ("w", 24, (HIDDEN, V_HEADS * 128), 0.0, 0.02))}
+        t = G.to_device(x, dev)
+        out = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(G.output_tail_workspace_bytes(rows, V_HEADS, HIDDEN), dtype=torch.uint8,
+                         device=dev)
+        fn = lambda: G.output_tail(t["o"], t["z"], t["gamma"], t["w"], out=out, workspace=ws,
+                                   stream=stream)
+        kern = fn
+        kbytes = HIDDEN * V_HEADS * 128 * 2 + 2 * rows * V_HEADS * 128 * 2 + rows * HIDDEN * 2
+        units, metric, kname = rows, "GDN dual-sequence output tail rows/sec (2x64)", "tail (prologue + cluster GEMM)"
+        desc = "output tail, 2 sequences x 64 rows, Hv=32 D=128 hidden=2048"
+
+    def timed(f, iters):
+        for _ in range(3):
+            flush.zero_()
+            f()
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(iters):
+            flush.zero_()          # evicts L2 (126 MB) before every step
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record(stream)
+            f()
+            e_.record(stream)
+            torch.cuda.synchronize()
+            total += s_.elapsed_time(e_)
+        return total / iters
+
+    with ClockSampler(0) as clocks:
+        ms = timed(fn, args.steps)
+    clk = clocks.summary()
+    k_ms = timed(kern, args.steps)
+    G.workspace_status(ws, stream)
+    gbs = kbytes / (k_ms * 1e-3) / 1e9
+    line = {
+        "metric": metric, "value": units / (ms * 1e-3), "unit": "tokens/s" if args.workload == "decode" else "rows/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": 3, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded SplitMix64/Box-Muller, benchmark distributions)",
+        "config": {"workload": desc, "l2": "flushed (256 MB written) before every step"},
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": gbs, "peak": hbm_peak,
+                     "unit": "GB/s", "frac": gbs / hbm_peak, "peak_kind": f"{peak_kind} copy",
+                     "algorithmic_bytes": kbytes, "kernel_ms": k_ms},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -174,6 +263,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["prefill", "decode", "tail"], default="prefill",
+                    help="prefill (default): the headline line; decode / tail: the other "
+                         "measured shapes on one GPU")
     ap.add_argument("--reduce", choices=["auto", "fused", "nccl"], default="auto",
                     help="N > 1: rank sum fused into the tail GEMM over NVLink peer memory, "
                          "or the unfused tail + a bf16 NCCL all-reduce; auto = fused for 2 "
@@ -182,6 +274,9 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload != "prefill":
+        run_secondary(args)
         return
 
     import numpy as np

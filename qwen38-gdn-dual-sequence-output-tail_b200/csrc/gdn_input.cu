@@ -9,11 +9,11 @@
 // and writes q, k and v in place of the split; a second kernel writes the
 // new conv state and a third splits a and b.
 //
-// Conv arithmetic (the CPU restatement does the same): for channel c and
+// Conv arithmetic (the CPU restatement sums the same way): for channel c and
 // token t, acc = w0 x[t-3]; acc = fma(w1, x[t-2], acc); acc = fma(w2,
-// x[t-1], acc); acc = fma(w3, x[t], acc); out = bf16(acc / (1 + exp(-acc))),
-// with rows before a sequence taken from its conv state (zero when the call
-// has no context).
+// x[t-1], acc); acc = fma(w3, x[t], acc); out = bf16(acc / (1 + exp(-acc)))
+// with the fast exp and divide (as the tail prologue's SiLU), rows before a
+// sequence taken from its conv state (zero when the call has no context).
 #include <algorithm>
 
 #include "gdn_common.cuh"
@@ -39,9 +39,13 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   f[6] = bf16lo_f32(v.w); f[7] = bf16hi_f32(v.w);
 }
 
-// One thread: 8 channels (16 bytes) x the tokens of one 64-token chunk of a
-// sequence, with a sliding window of the three previous rows.
-// grid (channels / 8 / blockDim.x, chunks).
+// Tokens per thread: a quarter of a 64-token chunk, all of its rows loaded
+// before the first is used (16 loads in flight per thread).
+constexpr int kConvRun = 16;
+
+// One thread: 8 channels (16 bytes) x a run of kConvRun tokens of one chunk of
+// a sequence, with a sliding window of the three previous rows.
+// grid (channels / 8 / blockDim.x, chunks * 64 / kConvRun).
 __global__ void __launch_bounds__(128)
 causal_conv_split_kernel(const __grid_constant__ ChunkTable tab,
                          const uint16_t* __restrict__ qkv, const uint16_t* __restrict__ w,
@@ -51,11 +55,20 @@ causal_conv_split_kernel(const __grid_constant__ ChunkTable tab,
   const int channels = 2 * qk_dim + v_dim;
   const int c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c8 >= channels) return;
-  const int chunk = blockIdx.y;
+  constexpr int kRunsPerChunk = kChunk / kConvRun;
+  const int chunk = blockIdx.y / kRunsPerChunk;
   const int seq = seq_of_chunk(tab, chunk);
   const int s0 = tab.cu[seq];
-  const int t0 = s0 + (chunk - tab.chunk_start[seq]) * kChunk;
-  const int t1 = min(t0 + kChunk, tab.cu[seq + 1]);
+  const int t0 = s0 + (chunk - tab.chunk_start[seq]) * kChunk +
+                 (blockIdx.y % kRunsPerChunk) * kConvRun;
+  const int t1 = min(t0 + kConvRun, tab.cu[seq + 1]);
+  if (t0 >= t1) return;
+  uint4 rows[kConvRun];
+#pragma unroll
+  for (int i = 0; i < kConvRun; ++i)
+    rows[i] = t0 + i < t1
+                  ? *reinterpret_cast<const uint4*>(qkv + static_cast<int64_t>(t0 + i) * channels + c8)
+                  : make_uint4(0u, 0u, 0u, 0u);
 
   float wt[4][8];
 #pragma unroll
@@ -84,9 +97,12 @@ causal_conv_split_kernel(const __grid_constant__ ChunkTable tab,
   else if (c8 < 2 * qk_dim) { dst = k; dst_stride = qk_dim; col = c8 - qk_dim; }
   else { dst = v; dst_stride = v_dim; col = c8 - 2 * qk_dim; }
 
-  for (int t = t0; t < t1; ++t) {
+#pragma unroll
+  for (int i = 0; i < kConvRun; ++i) {
+    const int t = t0 + i;
+    if (t >= t1) break;
     float x[8];
-    unpack8(*reinterpret_cast<const uint4*>(qkv + static_cast<int64_t>(t) * channels + c8), x);
+    unpack8(rows[i], x);
     float y[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -94,7 +110,7 @@ causal_conv_split_kernel(const __grid_constant__ ChunkTable tab,
       acc = fmaf(wt[1][e], h[1][e], acc);
       acc = fmaf(wt[2][e], h[2][e], acc);
       acc = fmaf(wt[3][e], x[e], acc);
-      y[e] = acc / (1.0f + expf(-acc));
+      y[e] = __fdividef(acc, 1.0f + __expf(-acc));
       h[0][e] = h[1][e];
       h[1][e] = h[2][e];
       h[2][e] = x[e];
@@ -203,7 +219,7 @@ cudaError_t launch_input_side(const ChunkTable& tab, const uint16_t* x, const ui
     if (e != cudaSuccess) return e;
     e = launch_tail_gemm(x, w_ab, ab, gemm_ws, tokens, n_ab, hidden, err, stream);
     if (e != cudaSuccess) return e;
-    dim3 cgrid((groups + 127) / 128, tab.total_chunks);
+    dim3 cgrid((groups + 127) / 128, tab.total_chunks * (kChunk / kConvRun));
     causal_conv_split_kernel<<<cgrid, 128, 0, stream>>>(tab, qkv, conv_w, conv_state, use_state,
                                                         q, k, v, qk_dim, v_dim);
     e = cudaGetLastError();
