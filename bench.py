@@ -45,7 +45,7 @@ CHUNK_MFLOP = 11.62    # prefill core work per (chunk of 64, v-head)
 # DRAM bytes (read + write) per call of the chunk core on the single-GPU
 # workload, from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum
 # of the prep and state kernels on this workload).
-CHUNK_CORE_DRAM_BYTES = {"prep": 68445696 + 121025792, "state": 244360448 + 44962816}
+CHUNK_CORE_DRAM_BYTES = {"prep": 68933888 + 121297152, "state": 244374272 + 46572032}
 
 
 def load_peaks():
