@@ -124,7 +124,8 @@ int32_t gdn_b200_output_tail(const void* o, const void* z, const void* gamma, co
                                 eps, s);
   if (e != cudaSuccess) return cuda_status(e, "tail prologue launch");
   e = gdn::launch_tail_gemm(gated, static_cast<const uint16_t*>(w_out),
-                            static_cast<uint16_t*>(out), gemm_ws, rows, hidden, K, err, s);
+                            static_cast<uint16_t*>(out), gemm_ws, rows, hidden, K, err, s,
+                            /*overlap_previous=*/true);
   return cuda_status(e, "tail GEMM launch");
 }
 
@@ -418,7 +419,7 @@ static int32_t layer_forward_impl(const gdn::ChunkTable& tab, const void* q, con
   }
   e = gdn::launch_tail_gemm(gated, static_cast<const uint16_t*>(w_out),
                             static_cast<uint16_t*>(out), gemm_ws, T, hidden, static_cast<int>(K),
-                            err, s);
+                            err, s, /*overlap_previous=*/true);
   return cuda_status(e, "tail GEMM launch");
 }
 

@@ -67,6 +67,18 @@ __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the previous kernel on its stream still
+// runs; griddep_wait() returns once that kernel has completed and its
+// writes are visible (a no-op for an ordinary launch).
+// griddep_launch_dependents() lets such a next kernel start early.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Waits until the flag has reached `epoch` (wrap-safe comparison), bounded
 // by the same wall-clock limit as every other wait; on expiry records
 // kErrWaitTimeout and returns false.
@@ -262,6 +274,27 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
           "r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  return remote;
+}
+
+// 1-D bulk copy from this CTA's shared memory into another CTA's shared
+// memory in the cluster; completion is counted as transaction bytes on the
+// destination's mbarrier (remote_bar, a cluster address).  Addresses
+// 16-byte aligned, bytes a multiple of 16.  The source must stay unchanged
+// until the destination has seen the bytes arrive.
+__device__ __forceinline__ void bulk_push_cluster(uint32_t remote_dst, const void* smem_src,
+                                                  uint32_t bytes, uint32_t remote_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(remote_dst),
+      "r"(smem_u32(smem_src)), "r"(bytes), "r"(remote_bar)
       : "memory");
 }
 

@@ -48,6 +48,7 @@ gdn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k
                   uint16_t* __restrict__ o_out, const uint16_t* __restrict__ z,
                   const uint16_t* __restrict__ gamma, uint16_t* __restrict__ gated_out,
                   const uint64_t* __restrict__ state_rows, int qk_heads, int value_heads) {
+  griddep_launch_dependents();   // the tail GEMM may start streaming W now
   const int h = blockIdx.x;
   const int seq = blockIdx.y;
   const int warp = threadIdx.x >> 5;

@@ -34,8 +34,12 @@ uint64_t tail_gemm_workspace_bytes(int64_t M, int N, int K);
 cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uint16_t* gamma,
                                  uint16_t* gated, int64_t rows, int value_heads, float eps,
                                  cudaStream_t stream);
+// overlap_previous: the previous launch on `stream` is one of this
+// library's kernels (tail prologue or decode) that writes `a` but not `w`;
+// for M <= 128 the GEMM then starts while it runs and streams W early.
 cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out, float* ws,
-                             int64_t M, int N, int K, uint32_t* err, cudaStream_t stream);
+                             int64_t M, int N, int K, uint32_t* err, cudaStream_t stream,
+                             bool overlap_previous = false);
 
 // Input side: projections, causal conv + SiLU, q/k/v split, conv-state
 // update (gdn_input.cu).  a, b come from one GEMM over [w_a; w_b] padded to

@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(256)
 tail_prologue_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ z,
                      const uint16_t* __restrict__ gamma, uint16_t* __restrict__ gated,
                      int64_t pairs, float eps) {
+  griddep_launch_dependents();   // the tail GEMM may start streaming W now
   const int64_t pair = static_cast<int64_t>(blockIdx.x) * 16 + (threadIdx.x >> 4);
   const int sub = threadIdx.x & 15;
   const bool live = pair < pairs;
@@ -229,24 +230,39 @@ tail_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
 // ------------------------------------------------- split-K in a cluster --
 // For M <= 128 (decode rows, the 2x64 dual tail) the K dimension is split
-// over the CTAs of one thread-block cluster (one CTA per split, up to 8).
-// Each CTA keeps its f32 partial tile in its own shared memory; after a
-// cluster barrier every CTA sums a slice of rows over the CTAs' tiles in
-// split order through distributed shared memory (deterministic) and writes
-// bf16.  No partial leaves the SMs and no second kernel runs.
-// N tile of the cluster path: 256 columns, so that the clusters of 8 of a
-// 2048-wide output (8 of them) are all resident at once.
-constexpr int kClusterBN = 256;
+// over the CTAs of one thread-block cluster (one CTA per split, up to 4) and
+// N into 64-column tiles, so a 2048-wide output runs as 32 clusters of 4 =
+// 128 CTAs, one per SM and all resident at once, each streaming an equal
+// share of W (the HBM stream).  Each CTA drains its f32 partial tile from
+// TMEM into its own shared memory; after a cluster barrier it pushes row
+// slice p of that tile to CTA p of the cluster with one bulk shared->shared
+// copy (the bytes are counted on p's mbarrier), and CTA p sums its slice over
+// the splits in split order (deterministic) and writes bf16.  No partial
+// leaves the SMs and no second kernel runs.
+//
+// The shape follows measured limits: the SM-to-SM network moves about 25-30
+// GB/s per SM, so the exchanged volume ((splits-1)/splits of a 128 x BN f32
+// tile) has to stay small, and at most 15 clusters of 8 CTAs of this size are
+// resident on a 148-SM B200, so 8-way splits of 128-column tiles would run
+// in two waves.
+constexpr int kClusterBN = 64;
+constexpr int kClusterStages = 8;
+constexpr int kClusterMaxSplits = 4;
 
-template <int BN>
+template <int BN, int Stages>
 struct ClusterGemmSmem {
   static constexpr int kPartStride = BN + 4;   // f32 per partial-tile row (padded)
   static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;
   static constexpr uint32_t kBBytes = BN * kGemmBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kBarrierOffset = kGemmStages * kStageBytes;
+  // After the main loop: the partial tile at 0, then the slices received
+  // from the other splits ([splits][slice rows][kPartStride], at most one
+  // tile's worth: splits * ceil(M / splits) <= 128 for splits dividing 128).
+  static constexpr uint32_t kPartBytes = kGemmBM * kPartStride * 4;
+  static constexpr uint32_t kRecvOffset = kPartBytes;
+  static constexpr uint32_t kBarrierOffset = Stages * kStageBytes;
   static constexpr uint32_t kTotal = kBarrierOffset + 256 + 1024;
-  static_assert(kGemmBM * kPartStride * 4 <= kBarrierOffset, "partial tile fits the stages");
+  static_assert(2 * kPartBytes <= kBarrierOffset, "partial tile and slices fit the stages");
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -265,48 +281,43 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t local_addr, uint32_t rank) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(remote)
-               : "memory");
-  return v;
-}
 
-template <int BN>
+template <int BN, int Stages>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 tail_gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b, uint16_t* __restrict__ out,
-                         int M, int N, int kblocks_total, int kblocks_per_split, uint32_t* err) {
-  using L = ClusterGemmSmem<BN>;
+                         int M, int N, int kblocks_total, int kblocks_per_split, int weights_first,
+                         uint32_t* err) {
+  using L = ClusterGemmSmem<BN, Stages>;
   constexpr int kPartStride = L::kPartStride;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
-  uint64_t* empty = full + kGemmStages;
-  uint64_t* tfull = empty + kGemmStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  uint64_t* empty = full + Stages;
+  uint64_t* tfull = empty + Stages;
+  uint64_t* recv = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv + 1);
   float* part = reinterpret_cast<float*>(smem);   // reuses the stages once the MMAs are done
+  float* slices = reinterpret_cast<float*>(smem + L::kRecvOffset);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t split = cluster_rank();
   const uint32_t splits = cluster_size();
   const int tn = blockIdx.x / splits;
-  const int tm = blockIdx.y;
   const int kb0 = static_cast<int>(split) * kblocks_per_split;
   const int kb1 = min(kb0 + kblocks_per_split, kblocks_total);
+  // Rows per slice: M spread evenly over the splits.
+  const int rows_per = (M + static_cast<int>(splits) - 1) / static_cast<int>(splits);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGemmStages; ++s) {
+    for (int s = 0; s < Stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
+    mbar_init(recv, 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
@@ -321,13 +332,31 @@ tail_gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmap_a,
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      int kb = kb0;
+      if (weights_first) {
+        // Launched to overlap the kernel before it on the stream, which
+        // wrote A but not W: fill the ring's W halves first, then wait for
+        // that kernel and load the A halves.
+        const int pre = min(Stages, kb1 - kb0);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], L::kStageBytes);
+          tma_load_2d(smem + i * L::kStageBytes + L::kABytes, &tmap_b, &full[i],
+                      (kb0 + i) * kGemmBK, tn * BN);
+        }
+        griddep_wait();
+        for (int i = 0; i < pre; ++i)
+          tma_load_2d(smem + i * L::kStageBytes, &tmap_a, &full[i], (kb0 + i) * kGemmBK, 0);
+        kb = kb0 + pre;
+        stage = pre % Stages;
+        phase = pre == Stages ? 1u : 0u;
+      }
+      for (; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, err)) break;
         mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
         uint8_t* sa = smem + stage * L::kStageBytes;
-        tma_load_2d(sa, &tmap_a, &full[stage], kb * kGemmBK, tm * kGemmBM);
+        tma_load_2d(sa, &tmap_a, &full[stage], kb * kGemmBK, 0);
         tma_load_2d(sa + L::kABytes, &tmap_b, &full[stage], kb * kGemmBK, tn * BN);
-        if (++stage == kGemmStages) { stage = 0; phase ^= 1u; }
+        if (++stage == Stages) { stage = 0; phase ^= 1u; }
       }
     }
     __syncwarp();
@@ -346,64 +375,80 @@ tail_gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmap_a,
           umma_bf16(tmem_base, umma_sdesc(sa + kk * 32, 16, 1024), umma_sdesc(sb + kk * 32, 16, 1024),
                     idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
         umma_commit(&empty[stage]);
-        if (++stage == kGemmStages) { stage = 0; phase ^= 1u; }
+        if (++stage == Stages) { stage = 0; phase ^= 1u; }
       }
       umma_commit(tfull);   // also covers a split with no k-block
     }
     __syncwarp();
   } else {
-    // Warps 2..5: TMEM lanes 32*(w%4) .. +31 -> rows of the partial tile.
+    // Warps 2..5: TMEM lanes 32*(w%4) .. +31 -> rows of the partial tile;
+    // rows at or beyond M are never summed and are left alone.
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const bool done = mbar_wait(tfull, 0, err);
     tmem_fence_after();
-    float* prow = part + row * kPartStride;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      uint32_t r[16];
-      tmem_ld16(tmem_addr(tmem_base, quarter * 32, c), r);
-      tmem_ld_wait();
+    if (quarter * 32 < M) {
+      float* prow = part + row * kPartStride;
       const bool live = done && kb1 > kb0;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem_addr(tmem_base, quarter * 32, c), r);
+        tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        reinterpret_cast<float4*>(prow + c)[j] =
-            live ? make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]))
-                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < 4; ++j)
+          reinterpret_cast<float4*>(prow + c)[j] =
+              live ? make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      fence_proxy_async_smem();   // the bulk copies below read these rows
     }
   }
-  cluster_sync_all();   // every partial tile written
+  cluster_sync_all();   // every partial tile written, every CTA's stages idle
 
-  // Rows [split * 128 / splits, +128 / splits) of the tile: sum the splits'
-  // partials in split order, round to bf16.
-  {
-    const int rows_per = kGemmBM / static_cast<int>(splits);
-    const int r0 = static_cast<int>(split) * rows_per;
-    const uint32_t pbase = smem_u32(part);
-    for (int idx = threadIdx.x; idx < rows_per * (BN / 4); idx += kGemmThreads) {
-      const int rr = r0 + idx / (BN / 4);
+  // Slice p = rows [p * rows_per, +rows_per) of the tile belongs to CTA p
+  // (rows at or beyond M ride along and are not written).
+  const int r0 = static_cast<int>(split) * rows_per;
+  const uint32_t slice_floats = static_cast<uint32_t>(rows_per * kPartStride);
+  const uint32_t slice_bytes = slice_floats * 4u;
+  if (threadIdx.x == 0) {
+    if (r0 < M && splits > 1) mbar_arrive_expect_tx(recv, (splits - 1u) * slice_bytes);
+    for (uint32_t p = 0; p < splits; ++p) {
+      if (p == split || static_cast<int>(p) * rows_per >= M) continue;
+      bulk_push_cluster(cluster_map(smem_u32(slices + split * slice_floats), p),
+                        part + p * slice_floats, slice_bytes, cluster_map(smem_u32(recv), p));
+    }
+  }
+  if (r0 < M) {
+    const bool got = splits == 1 || mbar_wait(recv, 0, err);
+    const int rows = min(rows_per, M - r0);
+    for (int idx = threadIdx.x; idx < rows * (BN / 4); idx += kGemmThreads) {
+      const int rr = idx / (BN / 4);
       const int c4 = idx % (BN / 4);
-      const uint32_t a = pbase + static_cast<uint32_t>((rr * kPartStride + c4 * 4) * 4);
-      // All remote loads in flight at once, then the sum in split order.
-      float4 v[8];
+      // All splits' values loaded, then the sum in split order.
+      float4 v[kClusterMaxSplits];
 #pragma unroll
-      for (uint32_t s = 0; s < 8; ++s)
-        v[s] = (s < splits) ? ld_cluster_f4(a, s) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (uint32_t s = 0; s < static_cast<uint32_t>(kClusterMaxSplits); ++s) {
+        const float* src = (s == split) ? part + (r0 + rr) * kPartStride
+                                        : slices + s * slice_floats + rr * kPartStride;
+        v[s] = (s < splits) ? reinterpret_cast<const float4*>(src)[c4]
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
       float4 acc = v[0];
 #pragma unroll
-      for (uint32_t s = 1; s < 8; ++s) {
+      for (uint32_t s = 1; s < static_cast<uint32_t>(kClusterMaxSplits); ++s) {
         if (s < splits) { acc.x += v[s].x; acc.y += v[s].y; acc.z += v[s].z; acc.w += v[s].w; }
       }
-      const int grow = tm * kGemmBM + rr;
-      if (grow < M) {
+      if (got) {
         uint2 w;
         w.x = pack_bf16x2(acc.x, acc.y);
         w.y = pack_bf16x2(acc.z, acc.w);
-        *reinterpret_cast<uint2*>(out + static_cast<int64_t>(grow) * N + tn * BN + c4 * 4) = w;
+        *reinterpret_cast<uint2*>(out + static_cast<int64_t>(r0 + rr) * N + tn * BN + c4 * 4) = w;
       }
     }
   }
-  cluster_sync_all();   // no CTA leaves while another still reads its tile
+  cluster_sync_all();   // every push has landed before any CTA leaves
 
   tmem_fence_before();
   __syncthreads();
@@ -484,15 +529,16 @@ int sm_count() {
 TailGemmPlan plan_tail_gemm(int64_t M, int N, int K) {
   TailGemmPlan p{};
   if (M <= kGemmBM && N % kClusterBN == 0) {
-    // One row tile: N tiles of 128 columns, K split over a cluster of up to
-    // 8 CTAs (the largest power of two that divides the k-blocks).
+    // One row tile: N tiles of kClusterBN columns, K split over a cluster of
+    // up to kClusterMaxSplits CTAs (the largest power of two that divides
+    // the k-blocks).
     p.cluster = true;
     p.bn = kClusterBN;
     p.tiles_m = 1;
     p.tiles_n = N / kClusterBN;
     p.kblocks_total = K / kGemmBK;
     p.splits = 1;
-    for (int sp = 8; sp >= 2; sp >>= 1) {
+    for (int sp = kClusterMaxSplits; sp >= 2; sp >>= 1) {
       if (p.kblocks_total % sp == 0) { p.splits = sp; break; }
     }
     p.kblocks_per_split = p.kblocks_total / p.splits;
@@ -554,15 +600,16 @@ static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, 
 // out[M, N] = a[M, K] @ w[N, K]^T  (bf16 in, f32 accumulate, bf16 out).
 // ws: f32 [M, N] scratch when the plan splits K (tail_gemm_workspace_bytes).
 cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out, float* ws,
-                             int64_t M, int N, int K, uint32_t* err, cudaStream_t stream) {
+                             int64_t M, int N, int K, uint32_t* err, cudaStream_t stream,
+                             bool overlap_previous) {
   if (M == 0) return cudaSuccess;
   const TailGemmPlan p = plan_tail_gemm(M, N, K);
   CUtensorMap ta, tb;
   if (!make_tmap_bf16(&ta, a, M, K, kGemmBM) || !make_tmap_bf16(&tb, w, N, K, p.bn))
     return cudaErrorInvalidValue;
   if (p.cluster) {
-    const uint32_t smem = ClusterGemmSmem<kClusterBN>::kTotal;
-    cudaError_t ec = cudaFuncSetAttribute(tail_gemm_cluster_kernel<kClusterBN>,
+    const uint32_t smem = ClusterGemmSmem<kClusterBN, kClusterStages>::kTotal;
+    cudaError_t ec = cudaFuncSetAttribute(tail_gemm_cluster_kernel<kClusterBN, kClusterStages>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (ec != cudaSuccess) return ec;
     cudaLaunchConfig_t cfg = {};
@@ -570,15 +617,18 @@ cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out
     cfg.blockDim = dim3(kGemmThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = static_cast<unsigned>(p.splits);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tail_gemm_cluster_kernel<kClusterBN>, ta, tb, out, static_cast<int>(M), N,
-                              p.kblocks_total, p.kblocks_per_split, err);
+    cfg.numAttrs = overlap_previous ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, tail_gemm_cluster_kernel<kClusterBN, kClusterStages>, ta, tb,
+                              out, static_cast<int>(M), N, p.kblocks_total, p.kblocks_per_split,
+                              overlap_previous ? 1 : 0, err);
   }
   cudaError_t e = (p.bn == 256)   ? launch_gemm_bn<256>(ta, tb, out, ws, M, N, p, err, stream)
                   : (p.bn == 128) ? launch_gemm_bn<128>(ta, tb, out, ws, M, N, p, err, stream)

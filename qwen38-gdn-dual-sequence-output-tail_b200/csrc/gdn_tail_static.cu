@@ -109,7 +109,8 @@ extern "C" GDN_B200_API int32_t gdn_b200_output_tail_no_alloc(
   if (e != cudaSuccess)
     return fail(STATECENTRIC_QWEN38_INTERNAL, std::string("launch: ") + cudaGetErrorString(e));
   e = gdn::launch_tail_gemm(gated, static_cast<const uint16_t*>(w_out), static_cast<uint16_t*>(out),
-                            partials, rows, hidden, static_cast<int>(K), err, s);
+                            partials, rows, hidden, static_cast<int>(K), err, s,
+                            /*overlap_previous=*/true);
   if (e != cudaSuccess)
     return fail(STATECENTRIC_QWEN38_INTERNAL, std::string("launch: ") + cudaGetErrorString(e));
   return STATECENTRIC_QWEN38_OK;
