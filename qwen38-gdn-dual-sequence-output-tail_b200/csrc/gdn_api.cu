@@ -72,9 +72,10 @@ int32_t gdn_b200_workspace_status(const void* workspace, void* stream) {
   e = cudaMemcpy(&word, workspace, sizeof(word), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_status(e, "cudaMemcpy(error word)");
   if (word == gdn::kErrNone) return ok();
-  const char* what = word == gdn::kErrWaitTimeout ? "a kernel wait ran out of time"
-                     : word == gdn::kErrTmemAlloc ? "TMEM allocation failed"
-                                                  : "kernel reported a geometry error";
+  const char* what = word == gdn::kErrWaitTimeout  ? "a kernel wait ran out of time"
+                     : word == gdn::kErrTmemAlloc  ? "TMEM allocation failed"
+                     : word == gdn::kErrMisaligned ? "a state row address is not 16-byte aligned"
+                                                   : "kernel reported a geometry error";
   return fail(STATECENTRIC_QWEN38_INTERNAL, std::string("device error: ") + what);
 }
 
@@ -406,7 +407,7 @@ static int32_t layer_forward_impl(const gdn::ChunkTable& tab, const void* q, con
                            static_cast<const uint16_t*>(v), static_cast<const uint16_t*>(a),
                            static_cast<const uint16_t*>(b), A_log, dt_bias, state, nullptr,
                            static_cast<const uint16_t*>(z), static_cast<const uint16_t*>(gamma),
-                           gated, tab.num_seqs, qk_heads, value_heads, s);
+                           gated, tab.num_seqs, qk_heads, value_heads, s, nullptr, err);
     if (e != cudaSuccess) return cuda_status(e, "decode launch");
   } else {
     const int32_t r = chunk_prefill_impl(tab, q, k, v, a, b, A_log, dt_bias, state, o, qk_heads,

@@ -25,6 +25,7 @@ enum : uint32_t {
   kErrWaitTimeout = 1,
   kErrTmemAlloc = 2,
   kErrBadGeometry = 3,
+  kErrMisaligned = 4,   // a device-side address (a state row) not 16-byte aligned
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -28,7 +28,10 @@ cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* 
                           const float* dt_bias, float* state, uint16_t* o_out,
                           const uint16_t* z, const uint16_t* gamma, uint16_t* gated_out,
                           int batch, int qk_heads, int value_heads, cudaStream_t stream,
-                          const uint64_t* state_rows = nullptr);
+                          const uint64_t* state_rows = nullptr, uint32_t* err = nullptr);
+
+// Streaming multiprocessors of the current device.
+int sm_count();
 
 uint64_t tail_gemm_workspace_bytes(int64_t M, int N, int K);
 cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uint16_t* gamma,

@@ -86,7 +86,7 @@ def test_flat_tail_equals_per_sequence_tails(cuda):
 
 # ---------------------------------------------------------------- decode --
 
-@pytest.mark.parametrize("batch", [1, 4, 64])
+@pytest.mark.parametrize("batch", [1, 4, 64, 100])
 def test_decode_step_matches_oracle(cuda, batch):
     import torch
     geom = G.Geometry(16, 32, 2048)
