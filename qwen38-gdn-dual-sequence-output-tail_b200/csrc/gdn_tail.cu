@@ -30,47 +30,66 @@ namespace gdn {
 
 // gated[r, h*128 + j] = bf16( bf16(o*rstd*gamma) * bf16(SiLU(z)) ); the
 // rounding points are the aclnn operator boundaries.  Sixteen threads per
-// (row, head), eight elements (16 bytes) each.
+// (row, head), eight elements (16 bytes) each; for large inputs every
+// thread takes kPairs (row, head) pairs kPrologueStride apart and issues all
+// of their loads before the first use, so more bytes are in flight per
+// thread (small inputs keep one pair per thread and twice the blocks).
+constexpr int kPrologueStride = 16;          // pairs per block per round (256 threads / 16)
+constexpr int64_t kPrologueTwoPairs = 65536; // from this many pairs on, two per thread
+
+template <int kProloguePairs>
 __global__ void __launch_bounds__(256)
 tail_prologue_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ z,
                      const uint16_t* __restrict__ gamma, uint16_t* __restrict__ gated,
                      int64_t pairs, float eps) {
   griddep_launch_dependents();   // the tail GEMM may start streaming W now
-  const int64_t pair = static_cast<int64_t>(blockIdx.x) * 16 + (threadIdx.x >> 4);
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kPrologueStride * kProloguePairs +
+                        (threadIdx.x >> 4);
   const int sub = threadIdx.x & 15;
-  const bool live = pair < pairs;
-  const int64_t base = (live ? pair : 0) * kHeadDim + sub * 8;
-  const uint4 ov = *reinterpret_cast<const uint4*>(o + base);
-  const uint4 zv = *reinterpret_cast<const uint4*>(z + base);
+  uint4 ov[kProloguePairs], zv[kProloguePairs];
+  int64_t base[kProloguePairs];
+  bool live[kProloguePairs];
+#pragma unroll
+  for (int i = 0; i < kProloguePairs; ++i) {
+    const int64_t pair = first + i * kPrologueStride;
+    live[i] = pair < pairs;
+    base[i] = (live[i] ? pair : 0) * kHeadDim + sub * 8;
+    ov[i] = *reinterpret_cast<const uint4*>(o + base[i]);
+    zv[i] = *reinterpret_cast<const uint4*>(z + base[i]);
+  }
   const uint4 gv = *reinterpret_cast<const uint4*>(gamma + sub * 8);
-  const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
-  const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
   const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-  float ss = 0.f;
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const float x0 = bf16lo_f32(ow[p]), x1 = bf16hi_f32(ow[p]);
-    ss += x0 * x0 + x1 * x1;
-  }
+  for (int i = 0; i < kProloguePairs; ++i) {
+    const uint32_t ow[4] = {ov[i].x, ov[i].y, ov[i].z, ov[i].w};
+    const uint32_t zw[4] = {zv[i].x, zv[i].y, zv[i].z, zv[i].w};
+    float ss = 0.f;
 #pragma unroll
-  for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  const float rstd = rsqrtf(ss * (1.0f / 128.0f) + eps);
-  uint32_t res[4];
-#pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    float r2[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float x = e ? bf16hi_f32(ow[p]) : bf16lo_f32(ow[p]);
-      const float zz = e ? bf16hi_f32(zw[p]) : bf16lo_f32(zw[p]);
-      const float gg = e ? bf16hi_f32(gw[p]) : bf16lo_f32(gw[p]);
-      const float nrm = round_bf16(x * rstd * gg);
-      const float sl = round_bf16(__fdividef(zz, 1.0f + __expf(-zz)));
-      r2[e] = nrm * sl;
+    for (int p = 0; p < 4; ++p) {
+      const float x0 = bf16lo_f32(ow[p]), x1 = bf16hi_f32(ow[p]);
+      ss += x0 * x0 + x1 * x1;
     }
-    res[p] = pack_bf16x2(r2[0], r2[1]);
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float rstd = rsqrtf(ss * (1.0f / 128.0f) + eps);
+    uint32_t res[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      float r2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float x = e ? bf16hi_f32(ow[p]) : bf16lo_f32(ow[p]);
+        const float zz = e ? bf16hi_f32(zw[p]) : bf16lo_f32(zw[p]);
+        const float gg = e ? bf16hi_f32(gw[p]) : bf16lo_f32(gw[p]);
+        const float nrm = round_bf16(x * rstd * gg);
+        const float sl = round_bf16(__fdividef(zz, 1.0f + __expf(-zz)));
+        r2[e] = nrm * sl;
+      }
+      res[p] = pack_bf16x2(r2[0], r2[1]);
+    }
+    if (live[i])
+      *reinterpret_cast<uint4*>(gated + base[i]) = make_uint4(res[0], res[1], res[2], res[3]);
   }
-  if (live) *reinterpret_cast<uint4*>(gated + base) = make_uint4(res[0], res[1], res[2], res[3]);
 }
 
 // ---------------------------------------------------------------- GEMM --
@@ -577,9 +596,15 @@ cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uin
                                  cudaStream_t stream) {
   const int64_t pairs = rows * value_heads;
   if (pairs == 0) return cudaSuccess;
-  const int64_t blocks = (pairs + 15) / 16;
-  tail_prologue_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(o, z, gamma, gated,
-                                                                          pairs, eps);
+  if (pairs >= kPrologueTwoPairs) {
+    const int64_t blocks = (pairs + 2 * kPrologueStride - 1) / (2 * kPrologueStride);
+    tail_prologue_kernel<2><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(o, z, gamma, gated,
+                                                                             pairs, eps);
+  } else {
+    const int64_t blocks = (pairs + kPrologueStride - 1) / kPrologueStride;
+    tail_prologue_kernel<1><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(o, z, gamma, gated,
+                                                                             pairs, eps);
+  }
   return cudaGetLastError();
 }
 
