@@ -407,7 +407,8 @@ static int32_t layer_forward_impl(const gdn::ChunkTable& tab, const void* q, con
                            static_cast<const uint16_t*>(v), static_cast<const uint16_t*>(a),
                            static_cast<const uint16_t*>(b), A_log, dt_bias, state, nullptr,
                            static_cast<const uint16_t*>(z), static_cast<const uint16_t*>(gamma),
-                           gated, tab.num_seqs, qk_heads, value_heads, s, nullptr, err);
+                           gated, tab.num_seqs, qk_heads, value_heads, s, nullptr, err,
+                           w_out, static_cast<uint64_t>(hidden) * K * 2);
     if (e != cudaSuccess) return cuda_status(e, "decode launch");
   } else {
     const int32_t r = chunk_prefill_impl(tab, q, k, v, a, b, A_log, dt_bias, state, o, qk_heads,

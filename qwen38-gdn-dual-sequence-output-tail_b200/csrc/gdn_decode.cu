@@ -101,7 +101,8 @@ gdn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k
                   uint16_t* __restrict__ o_out, const uint16_t* __restrict__ z,
                   const uint16_t* __restrict__ gamma, uint16_t* __restrict__ gated_out,
                   const uint64_t* __restrict__ state_rows, int units, int qk_heads,
-                  int value_heads, uint32_t* err) {
+                  int value_heads, const uint8_t* __restrict__ l2_pre, uint64_t l2_pre_bytes,
+                  uint32_t* err) {
   griddep_launch_dependents();   // the tail GEMM may start streaming W now
   extern __shared__ uint8_t smem_raw[];
   DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(
@@ -159,6 +160,18 @@ gdn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k
             bulk_load(reinterpret_cast<uint8_t*>(sm.state[s]) + p * (kUnitBytes / kUnitPieces),
                       reinterpret_cast<const uint8_t*>(g) + p * (kUnitBytes / kUnitPieces),
                       kUnitBytes / kUnitPieces, &sm.full[s]);
+          if (i == n - 1 && l2_pre != nullptr) {
+            // Last state load issued: warm L2 with this CTA's share of the
+            // buffer the next kernel reads (the tail GEMM's weight), while
+            // the remaining units drain.
+            const uint64_t per = ((l2_pre_bytes + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+            const uint64_t lim = per * (blockIdx.x + 1);
+            const uint64_t end = l2_pre_bytes < lim ? l2_pre_bytes : lim;
+            for (uint64_t off = per * blockIdx.x; off + 16 <= end; off += 32768) {
+              const uint64_t len = (end - off < 32768ull ? end - off : 32768ull) & ~15ull;
+              prefetch_l2(l2_pre + off, static_cast<uint32_t>(len));
+            }
+          }
         }
       }
       bulk_wait_all();   // every store has landed before the CTA leaves
@@ -285,7 +298,8 @@ cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* 
                           const float* dt_bias, float* state, uint16_t* o_out,
                           const uint16_t* z, const uint16_t* gamma, uint16_t* gated_out,
                           int batch, int qk_heads, int value_heads, cudaStream_t stream,
-                          const uint64_t* state_rows, uint32_t* err) {
+                          const uint64_t* state_rows, uint32_t* err, const void* l2_prefetch,
+                          uint64_t l2_prefetch_bytes) {
   const int units = batch * value_heads;
   if (units <= 0) return cudaSuccess;
   const uint32_t smem = decode_smem_bytes();
@@ -295,7 +309,7 @@ cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* 
   const int grid = units < sm_count() ? units : sm_count();
   gdn_decode_kernel<<<grid, kDecodeThreads, smem, stream>>>(
       q, k, v, a, b, A_log, dt_bias, state, o_out, z, gamma, gated_out, state_rows, units,
-      qk_heads, value_heads, err);
+      qk_heads, value_heads, static_cast<const uint8_t*>(l2_prefetch), l2_prefetch_bytes, err);
   return cudaGetLastError();
 }
 

@@ -28,7 +28,10 @@ cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* 
                           const float* dt_bias, float* state, uint16_t* o_out,
                           const uint16_t* z, const uint16_t* gamma, uint16_t* gated_out,
                           int batch, int qk_heads, int value_heads, cudaStream_t stream,
-                          const uint64_t* state_rows = nullptr, uint32_t* err = nullptr);
+                          const uint64_t* state_rows = nullptr, uint32_t* err = nullptr,
+                          const void* l2_prefetch = nullptr, uint64_t l2_prefetch_bytes = 0);
+// l2_prefetch: a buffer (16-byte aligned) the next kernel on the stream reads,
+// brought into L2 by the decode CTAs once their last state block is loading.
 
 // Streaming multiprocessors of the current device.
 int sm_count();
