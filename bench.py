@@ -59,58 +59,98 @@ def load_peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples the SM clock and the throttle reasons of one GPU while the timed
+    region runs: NVML polled every 2 ms from a thread (the timed regions here
+    are a few ms long), or nvidia-smi at its 20 ms period when NVML is absent."""
 
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
+    SMI_COLUMNS = {"hw_slowdown": 5, "hw_thermal_slowdown": 6, "sw_thermal_slowdown": 7,
+                   "sw_power_cap": 8}
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index: int):
         self.device_index = device_index
+        self.samples = []      # (sm_mhz, max_mhz, reason bit mask)
         self.proc = None
         self.file = None
+        self.thread = None
+        self.stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [v.strip() for v in visible.split(",") if v.strip()]
+        if ids and self.device_index < len(ids) and ids[self.device_index].isdigit():
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(int(ids[self.device_index]))
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
+
+    def _poll(self, nv, h):
+        reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx,
+                                     int(reasons(h))))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
-        self.file = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.file, stderr=subprocess.DEVNULL)
+            nv, h = self._nvml_handle()
+            self.thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
+            self.thread.start()
         except Exception:
-            self.proc = None
-        time.sleep(0.3)
+            self.thread = None
+            self.file = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
+                     "--format=csv,noheader,nounits", "-lms", "20"],
+                    stdout=self.file, stderr=subprocess.DEVNULL)
+            except Exception:
+                self.proc = None
+        time.sleep(0.05)
         return self
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-        self.file.flush()
+        if self.file is not None:
+            self.file.flush()
+            try:
+                with open(self.file.name) as f:
+                    for r in (r.split(",") for r in f.read().strip().splitlines() if r.strip()):
+                        try:
+                            mask = sum(self.REASONS[name] for name, col in self.SMI_COLUMNS.items()
+                                       if r[col].strip().lower() == "active")
+                            self.samples.append((float(r[1]), float(r[2]), mask))
+                        except Exception:
+                            continue
+                os.unlink(self.file.name)
+            except Exception:
+                pass
 
     def summary(self):
-        try:
-            with open(self.file.name) as f:
-                rows = [r.split(",") for r in f.read().strip().splitlines() if r.strip()]
-            os.unlink(self.file.name)
-        except Exception:
-            rows = []
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = max(mx, float(r[2]))
-                for i, name in enumerate(names):
-                    if r[5 + i].strip().lower() == "active":
-                        reasons.add(name)
-            except Exception:
-                continue
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": mx or None, "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [x[0] for x in self.samples]
+        mx = max((x[1] for x in self.samples), default=0.0)
+        reasons = sorted(name for name, bit in self.REASONS.items()
+                         if any(x[2] & bit for x in self.samples))
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": reasons, "samples": len(sm),
+                "source": "nvml, 2 ms" if self.thread is not None else "nvidia-smi, 20 ms"}
 
 
 def workload_desc(nseq: int) -> str:
@@ -118,18 +158,38 @@ def workload_desc(nseq: int) -> str:
             f"Hk={QK_HEADS} Hv={V_HEADS} D=128 hidden={HIDDEN}, chunk 64")
 
 
-def cpu_oracle_prefill(seq_len: int, nseq: int, threads: int | None = None):
+def use_fused_reduce(world: int, reduce: str) -> bool:
+    return world > 1 and (reduce == "fused" or (reduce == "auto" and world == 2))
+
+
+def prefill_config(world: int, reduce: str) -> dict:
+    """The headline workload's config, the same for both arms."""
+    nseq = SEQS_PER_GPU * world
+    T = nseq * SEQ_LEN
+    hk, hv = QK_HEADS // world, V_HEADS // world
+    qkvz_mb = (2 * T * hk * 128 + 2 * T * hv * 128) * 2 / 1e6
+    fused = use_fused_reduce(world, reduce)
+    return {"workload": workload_desc(nseq), "tokens_per_step": T, "sequences": nseq,
+            "seq_len": SEQ_LEN,
+            "parallelism": f"head-parallel tp{world}" + (
+                "" if world == 1 else
+                " + rank sum fused into the tail GEMM (NVLink peer memory)" if fused
+                else " + nccl all-reduce"),
+            "l2": "inputs larger than L2 (q,k,v,z = %.0f MB per step)" % qkvz_mb}
+
+
+def cpu_oracle_prefill(seq_len: int, nseq: int):
     """Runs the CPU oracle (restatement of the reference's op sequence) on the
-    prefill workload; returns (tokens/s, seconds, threads)."""
+    prefill workload, with inputs from the oracle's own copy of the seeded
+    generator (the product library is never loaded); returns (tokens/s,
+    seconds, threads)."""
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    if threads:
-        os.environ["OMP_NUM_THREADS"] = str(threads)
     import gdn_oracle as O
-    import gdn_b200 as G
+    import gdn_b200 as G          # Geometry and the input layout only: no library load
     geom = G.Geometry(QK_HEADS, V_HEADS, HIDDEN)
     cu = np.arange(nseq + 1, dtype=np.int32) * seq_len
-    x = G.synthetic_layer_inputs(cu, geom, seed=1)
+    x = G.synthetic_layer_inputs(cu, geom, seed=1, fill=O.fill)
     st = x["state"].copy()
     t0 = time.perf_counter()
     O.layer(x["q"], x["k"], x["v"], x["a"], x["b"], x["z"], x["A_log"], x["dt_bias"],
@@ -139,6 +199,10 @@ def cpu_oracle_prefill(seq_len: int, nseq: int, threads: int | None = None):
 
 
 def run_reference(args):
+    """The reference arm: the CPU restatement of the reference's path (the
+    oracle; the reference itself runs only on Ascend NPUs) on all host threads.
+    Each step is the 2x4096 prefill of one GPU's share, a bounded sample of
+    the N-GPU workload; rank 0 alone runs it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -156,78 +220,35 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": workload_desc(nseq), "tokens_per_step": nseq * SEQ_LEN,
-                   "sequences": nseq, "seq_len": SEQ_LEN},
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded SplitMix64/Box-Muller, benchmark distributions)",
+        "config": prefill_config(args.gpus, args.reduce),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{SEQS_PER_GPU}x{SEQ_LEN} tokens of the "
-                                   f"{nseq}x{SEQ_LEN} workload per step"},
+                                   f"{nseq}x{SEQ_LEN} workload per step (median of "
+                                   f"{args.steps})"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_secondary(args):
-    """The other measured shapes of the benchmark, one GPU, one JSON line:
-    ``decode``: one decode step of B=64 sequences (f32 state [64, 32, 128,
-    128] ~ N(0, 0.05), resident; the state read and written is the HBM
-    stream) plus the flattened tail over the 64 rows; ``tail``: the
-    dual-sequence output tail over 2 x 64 rows (o, z [128, 32, 128], w_out
-    [2048, 4096]; the weight read is the HBM stream).  Each timed step is one
-    call, with a 256 MB buffer written between steps so that every step
-    starts with the state / weight out of L2."""
-    import numpy as np
-    import torch
-    import gdn_b200 as G
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    geom = G.Geometry(QK_HEADS, V_HEADS, HIDDEN)
-    stream = torch.cuda.Stream(device=dev)
-    torch.cuda.set_stream(stream)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    hbm_peak, tf_peak, peak_kind = load_peaks()
-    if args.workload == "decode":
-        B = 64
-        cu = np.arange(B + 1, dtype=np.int32)
-        t = G.to_device(G.synthetic_layer_inputs(cu, geom, seed=5, state_std=0.05), dev)
-        out = torch.empty(B, HIDDEN, dtype=torch.bfloat16, device=dev)
-        ws = torch.empty(G.layer_forward_workspace_bytes(cu, QK_HEADS, V_HEADS, HIDDEN),
-                         dtype=torch.uint8, device=dev)
-        fn = lambda: G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
-                                     t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu,
-                                     out=out, workspace=ws, stream=stream)
-        # the decode kernel alone (state read + write: the roofline stream)
-        gated = torch.empty(B, V_HEADS * 128, dtype=torch.bfloat16, device=dev)
-        kern = lambda: G.decode_step(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"],
-                                     t["dt_bias"], t["state"], z=t["z"], gamma=t["gamma"],
-                                     gated_out=gated, stream=stream)
-        kbytes = 2 * B * V_HEADS * 128 * 128 * 4
-        units, metric, kname = B, "GDN decode tokens/sec (B=64, one step + tail)", "gdn_decode_kernel"
-        desc = "decode step, 64 sequences x 1 token, Hk=16 Hv=32 D=128 hidden=2048"
-    else:
-        rows = 128
-        x = {n: G.fill(0, i, sh, G.NORMAL, mu, sd, G.BF16) for n, i, sh, mu, sd in (
-            ("o", 21, (rows, V_HEADS, 128), 0.0, 1.0), ("z", 22, (rows, V_HEADS, 128), 0.0, 1.0),
-            ("gamma", 23, (128,), 1.0, 0.02), ("w", 24, (HIDDEN, V_HEADS * 128), 0.0, 0.02))}
-        t = G.to_device(x, dev)
-        out = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
-        ws = torch.empty(G.output_tail_workspace_bytes(rows, V_HEADS, HIDDEN), dtype=torch.uint8,
-                         device=dev)
-        fn = lambda: G.output_tail(t["o"], t["z"], t["gamma"], t["w"], out=out, workspace=ws,
-                                   stream=stream)
-        kern = fn
-        kbytes = HIDDEN * V_HEADS * 128 * 2 + 2 * rows * V_HEADS * 128 * 2 + rows * HIDDEN * 2
-        units, metric, kname = rows, "GDN dual-sequence output tail rows/sec (2x64)", "tail (prologue + cluster GEMM)"
-        desc = "output tail, 2 sequences x 64 rows, Hv=32 D=128 hidden=2048"
+def nbytes(*tensors) -> int:
+    return sum(t.numel() * t.element_size() for t in tensors)
 
-    def timed(f, iters):
-        for _ in range(3):
+
+def flushed_timer(stream, flush):
+    """Times single calls on `stream` with CUDA events, writing `flush` (larger
+    than L2) before each, so every call starts with its inputs out of L2."""
+    import torch
+
+    def timed(f, iters, warm=3):
+        for _ in range(warm):
             flush.zero_()
             f()
         torch.cuda.synchronize()
         total = 0.0
         for _ in range(iters):
-            flush.zero_()          # evicts L2 (126 MB) before every step
+            flush.zero_()
             s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s_.record(stream)
             f()
@@ -235,25 +256,97 @@ def run_secondary(args):
             torch.cuda.synchronize()
             total += s_.elapsed_time(e_)
         return total / iters
+    return timed
 
-    with ClockSampler(0) as clocks:
-        ms = timed(fn, args.steps)
-    clk = clocks.summary()
-    k_ms = timed(kern, args.steps)
+
+def small_shape_components(dev, stream, iters):
+    """The metric's other shapes on one GPU, each timed per call with L2
+    flushed before the call:
+
+    * ``prefill_2x64``: the whole layer (chunked prefill + flattened tail) over
+      2 sequences of 64 tokens, the reference's admitted dual-sequence unit
+      (inputs as the 2x4096 workload, zero initial state);
+    * ``tail_2x64``: the dual-sequence output tail alone over 2 x 64 rows
+      (o, z [128, 32, 128] ~ N(0,1), gamma 1 + N(0, 0.02), w_out [2048, 4096]
+      ~ N(0, 0.02));
+    * ``decode_b64``: one decode step of 64 sequences (f32 state [64, 32, 128,
+      128] ~ N(0, 0.05)) plus the flattened tail over the 64 rows, and the
+      decode kernel alone (the state read + write is its HBM stream).
+
+    ``gbs`` = algorithmic bytes (every input read once, the state read and
+    written, the output written) / time; ``frac`` = gbs / measured HBM copy
+    bandwidth."""
+    import numpy as np
+    import torch
+    import gdn_b200 as G
+    hbm_peak, _, _ = load_peaks()
+    geom = G.Geometry(QK_HEADS, V_HEADS, HIDDEN)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    timed = flushed_timer(stream, flush)
+    comps = {}
+
+    def layer_case(cu, seed, state_std):
+        t = G.to_device(G.synthetic_layer_inputs(cu, geom, seed=seed, state_std=state_std), dev)
+        T = int(cu[-1])
+        out = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(G.layer_forward_workspace_bytes(cu, QK_HEADS, V_HEADS, HIDDEN),
+                         dtype=torch.uint8, device=dev)
+        fn = lambda: G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
+                                     t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu,
+                                     out=out, workspace=ws, stream=stream)
+        alg = (nbytes(*(t[n] for n in ("q", "k", "v", "a", "b", "z", "A_log", "dt_bias",
+                                       "gamma", "w_out"))) + 2 * nbytes(t["state"]) + nbytes(out))
+        return t, fn, ws, alg
+
+    # prefill 2 x 64
+    cu = np.array([0, 64, 128], np.int32)
+    _, fn, ws, alg = layer_case(cu, 1, 0.0)
+    ms = timed(fn, iters)
     G.workspace_status(ws, stream)
-    gbs = kbytes / (k_ms * 1e-3) / 1e9
-    line = {
-        "metric": metric, "value": units / (ms * 1e-3), "unit": "tokens/s" if args.workload == "decode" else "rows/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": 3, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded SplitMix64/Box-Muller, benchmark distributions)",
-        "config": {"workload": desc, "l2": "flushed (256 MB written) before every step"},
-        "roofline": {"bound": "hbm", "kernel": kname, "achieved": gbs, "peak": hbm_peak,
-                     "unit": "GB/s", "frac": gbs / hbm_peak, "peak_kind": f"{peak_kind} copy",
-                     "algorithmic_bytes": kbytes, "kernel_ms": k_ms},
-        "clocks": clk,
-    }
-    print(json.dumps(line), flush=True)
+    gbs = alg / (ms * 1e-3) / 1e9
+    comps["prefill_2x64"] = {"us": ms * 1e3, "tokens_per_s": 128 / (ms * 1e-3),
+                             "algorithmic_bytes": alg, "gbs": gbs, "frac": gbs / hbm_peak,
+                             "bound": "hbm"}
+
+    # output tail 2 x 64
+    rows = 128
+    x = {n: G.fill(0, i, sh, G.NORMAL, mu, sd, G.BF16) for n, i, sh, mu, sd in (
+        ("o", 21, (rows, V_HEADS, 128), 0.0, 1.0), ("z", 22, (rows, V_HEADS, 128), 0.0, 1.0),
+        ("gamma", 23, (128,), 1.0, 0.02), ("w", 24, (HIDDEN, V_HEADS * 128), 0.0, 0.02))}
+    t = G.to_device(x, dev)
+    out = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(G.output_tail_workspace_bytes(rows, V_HEADS, HIDDEN), dtype=torch.uint8,
+                     device=dev)
+    ms = timed(lambda: G.output_tail(t["o"], t["z"], t["gamma"], t["w"], out=out, workspace=ws,
+                                     stream=stream), iters)
+    G.workspace_status(ws, stream)
+    alg = nbytes(t["o"], t["z"], t["gamma"], t["w"], out)
+    gbs = alg / (ms * 1e-3) / 1e9
+    comps["tail_2x64"] = {"us": ms * 1e3, "rows_per_s": rows / (ms * 1e-3),
+                          "algorithmic_bytes": alg, "gbs": gbs, "frac": gbs / hbm_peak,
+                          "bound": "hbm"}
+
+    # decode B = 64: step (decode + tail) and the decode kernel alone
+    B = 64
+    cu = np.arange(B + 1, dtype=np.int32)
+    t, fn, ws, alg = layer_case(cu, 5, 0.05)
+    ms = timed(fn, iters)
+    G.workspace_status(ws, stream)
+    gated = torch.empty(B, V_HEADS * 128, dtype=torch.bfloat16, device=dev)
+    k_ms = timed(lambda: G.decode_step(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"],
+                                       t["dt_bias"], t["state"], z=t["z"], gamma=t["gamma"],
+                                       gated_out=gated, stream=stream), iters)
+    k_alg = (2 * nbytes(t["state"]) + nbytes(*(t[n] for n in ("q", "k", "v", "a", "b", "z",
+                                                               "A_log", "dt_bias", "gamma")))
+             + nbytes(gated))
+    gbs, k_gbs = alg / (ms * 1e-3) / 1e9, k_alg / (k_ms * 1e-3) / 1e9
+    comps["decode_b64"] = {"us": ms * 1e3, "tokens_per_s": B / (ms * 1e-3),
+                           "algorithmic_bytes": alg, "gbs": gbs, "frac": gbs / hbm_peak,
+                           "bound": "hbm", "kernel": "gdn_decode_kernel", "kernel_us": k_ms * 1e3,
+                           "kernel_algorithmic_bytes": k_alg, "kernel_gbs": k_gbs,
+                           "kernel_frac": k_gbs / hbm_peak}
+    del flush
+    return comps
 
 
 def main():
@@ -263,20 +356,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["prefill", "decode", "tail"], default="prefill",
-                    help="prefill (default): the headline line; decode / tail: the other "
-                         "measured shapes on one GPU")
+    ap.add_argument("--component-iters", type=int, default=50,
+                    help="calls timed per small-shape component (N=1 only)")
     ap.add_argument("--reduce", choices=["auto", "fused", "nccl"], default="auto",
                     help="N > 1: rank sum fused into the tail GEMM over NVLink peer memory, "
                          "or the unfused tail + a bf16 NCCL all-reduce; auto = fused for 2 "
                          "GPUs, NCCL from 4 (measured: 2 GPUs 0.523 vs 0.587 ms per step, "
                          "4 GPUs 0.904 vs 0.809)")
     args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
     if args.impl == "reference":
         run_reference(args)
-        return
-    if args.workload != "prefill":
-        run_secondary(args)
         return
 
     import numpy as np
@@ -307,9 +398,7 @@ def main():
     x = G.synthetic_layer_inputs(cu, geom, seed=1 + 1000 * rank)
     host = {}
     for n in ("q", "k", "v", "a", "b", "z"):
-        arr = x[n]
-        t = torch.from_numpy(arr.view(np.int16)).view(torch.bfloat16)
-        host[n] = t.pin_memory()
+        host[n] = torch.from_numpy(x[n].view(np.int16)).view(torch.bfloat16).pin_memory()
     t = G.to_device(x, dev)
     out = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device=dev)
     ws = torch.empty(G.layer_forward_workspace_bytes(cu, hk, hv, HIDDEN), dtype=torch.uint8,
@@ -319,7 +408,7 @@ def main():
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)
 
-    fused = world > 1 and (args.reduce == "fused" or (args.reduce == "auto" and world == 2))
+    fused = use_fused_reduce(world, args.reduce)
     group = None
     if fused:
         # Every rank's exchange region mapped into every rank (CUDA IPC
@@ -374,12 +463,13 @@ def main():
         step()
     torch.cuda.synchronize()
     G.workspace_status(ws_ar if fused else ws, stream)
+    launches0 = G.kernel_launches()
     with ClockSampler(local) as clocks:
         ms = timed(step, args.steps, 0)
+    launches = G.kernel_launches() - launches0
     clk = clocks.summary()
     G.workspace_status(ws_ar if fused else ws, stream)
-    tokens_total = T  # every rank sees all tokens of its shard; tokens are not duplicated
-    value = tokens_total / (ms * 1e-3)
+    value = T / (ms * 1e-3)   # T = every token of the job: ranks hold head shards of the same tokens
 
     # Components, timed alone with CUDA events on the launching stream:
     # the chunked core (prep + state kernels) and the output tail.
@@ -412,6 +502,7 @@ def main():
                                        xs["conv_w"], xs["conv_state"], cu, hk, out=in_out,
                                        workspace=ws_in, stream=stream), args.steps, 2)
     G.workspace_status(ws_in, stream)
+    del xs, ws_in, in_out
     hbm_peak, tf_peak, peak_kind = load_peaks()
     chunks = nseq * (SEQ_LEN // 64)
     core_flop = CHUNK_MFLOP * 1e6 * chunks * hv
@@ -437,6 +528,8 @@ def main():
                 "traffic_unit": "bytes per call (ncu, prep + state kernels)",
                 "traffic_gbs": (traffic / (comps[dom]["ms"] * 1e-3) / 1e9) if traffic else None,
                 "hbm_peak_gbs": hbm_peak}
+    if world == 1:
+        comps.update(small_shape_components(dev, stream, args.component_iters))
 
     # End to end through the provider ABI (the reference-facing plugin
     # interface), as a serving loop drives it: every step copies its inputs
@@ -445,11 +538,15 @@ def main():
     # sets and three streams (host->device copies, the provider's stream,
     # device->host copies), so the upload of step i+1 overlaps the compute and
     # read-back of step i; the recurrent state chains the steps in order on
-    # the provider's stream.
+    # the provider's stream.  With N GPUs each rank reads back only the rows
+    # it owns (rows [r T/N, (r+1) T/N) of the reduced output), so the job
+    # copies the output to the host once.
     prov = G.Provider(geom, max_tokens=T, world_size=world, rank=rank, device=local)
-    host_outs = [torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
-    d2h = host_outs[0].numel() * host_outs[0].element_size()
+    r0, r1 = rank * T // world, (rank + 1) * T // world
+    host_outs = [torch.empty(r1 - r0, HIDDEN, dtype=torch.bfloat16).pin_memory()
+                 for _ in range(2)]
+    h2d = nbytes(*host.values()) * world
+    d2h = T * HIDDEN * 2
     t_in = [t, dict(t)]
     for n in host:
         t_in[1][n] = torch.empty_like(t[n])
@@ -478,7 +575,7 @@ def main():
         ev_comp[b].record(stream)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_comp[b])
-            host_outs[b].copy_(outs[b], non_blocking=True)
+            host_outs[b].copy_(outs[b][r0:r1], non_blocking=True)
             ev_out[b].record(s_out)
         while len(pending) > 1:                 # keep one submission in flight
             ev = pending.pop(0)
@@ -517,27 +614,20 @@ def main():
                          f"({csec:.2f} s)"}
 
     if rank == 0:
-        workload = workload_desc(nseq)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded SplitMix64/Box-Muller, benchmark distributions)",
-            "config": {"workload": workload, "tokens_per_step": T,
-                       "sequences": nseq, "seq_len": SEQ_LEN,
-                       "parallelism": f"head-parallel tp{world}" + (
-                           "" if world == 1 else
-                           " + rank sum fused into the tail GEMM (NVLink peer memory)" if fused
-                           else " + nccl all-reduce"),
-                       "l2": "inputs larger than L2 (q,k,v,z = %.0f MB per step)" %
-                             (sum(v.numel() * v.element_size() for n, v in t.items()
-                                  if n in ("q", "k", "v", "z")) / 1e6)},
+            "config": prefill_config(world, args.reduce),
             "roofline": roofline,
             "components": comps,
             "cpu_baseline": cpu,
             "e2e": {"value": T / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
-            "gpu_launches": 4 * args.steps,
+                    "d2h_bytes_per_step": d2h,
+                    "note": "whole-job bytes: every rank uploads its head shard's inputs, each "
+                            "output row is read back once by the rank that owns it"},
+            "gpu_launches": launches,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

@@ -4,8 +4,10 @@
  *
  * Every entry point takes device pointers, sizes and a cudaStream_t passed as
  * void*, enqueues its kernels on that stream and returns without waiting.
- * Nothing here allocates device memory: scratch space is passed in by the
- * caller (query its size with the matching *_workspace_bytes function).
+ * The compute entry points allocate no device memory: scratch space is passed
+ * in by the caller (query its size with the matching *_workspace_bytes
+ * function).  The one exception is gdn_b200_exchange_alloc(), which exists to
+ * allocate the IPC-shareable exchange region of the head-parallel tail.
  * Return values are the STATECENTRIC_QWEN38_* status codes of
  * statecentric_qwen38_provider_api_v1.h; gdn_b200_last_error() returns the
  * message of the last failure on the calling thread.
@@ -53,6 +55,12 @@ extern "C" {
 /* Message of the last failed call on this thread ("" when none). */
 GDN_B200_API const char* gdn_b200_last_error(void);
 
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads; a monotonically increasing count taken at each successful
+ * launch).  No counterpart in the reference: it lets a caller check how many
+ * device launches a step costs. */
+GDN_B200_API uint64_t gdn_b200_kernel_launches(void);
+
 /* Every entry point that takes a workspace keeps a device error word in its
  * first 256 bytes.  Kernels never spin without a time limit: a wait that runs
  * out records an error there and the kernel exits.  This call synchronises
@@ -81,8 +89,10 @@ GDN_B200_API int32_t gdn_b200_output_tail(const void* o, const void* z, const vo
  * sizes are limited to rows <= 128, value_heads * 128 <= 4096, hidden <= 2048
  * (larger sizes return INVALID_ARGUMENT).  All calls on a device share the
  * array: calls that overlap on the GPU race and must be serialised.  The
- * first call on a device resolves the array's device address; make it before
- * any stream capture. */
+ * first call in each CUDA context (per device, and again after
+ * cudaDeviceReset) resolves the array's device address; make it before any
+ * stream capture.  Argument errors are reported like every other entry point
+ * (status + gdn_b200_last_error()). */
 #define GDN_B200_NO_ALLOC_MAX_ROWS 128
 #define GDN_B200_NO_ALLOC_MAX_VALUE 4096
 #define GDN_B200_NO_ALLOC_MAX_HIDDEN 2048
@@ -92,6 +102,15 @@ GDN_B200_API int32_t gdn_b200_output_tail_no_alloc(const void* o, const void* z,
                                                    void* out, int64_t rows,
                                                    int32_t value_heads, int32_t hidden,
                                                    float eps, void* stream);
+
+/* Device-side status of the last gdn_b200_output_tail_no_alloc() call in the
+ * current context: synchronises `stream`, then reads the error word the
+ * kernels record in the static scratch (a bounded wait that ran out, a failed
+ * TMEM allocation).  Returns OK when nothing was recorded or no call has run
+ * in this context, INTERNAL with gdn_b200_last_error() naming the reason
+ * otherwise.  It is the no-workspace counterpart of
+ * gdn_b200_workspace_status() and allocates nothing either. */
+GDN_B200_API int32_t gdn_b200_output_tail_no_alloc_status(void* stream);
 
 /* One decode step for `batch` sequences of one token each: gating, q/k
  * L2-norm, S <- exp(g) S; S += beta k (v - S^T k)^T; o = scale S^T q,

@@ -487,3 +487,56 @@ ORACLE_EXPORT void gdn_oracle_causal_conv1d(const uint16_t* x, const uint16_t* w
     }
   }
 }
+
+/* ------------------------------------------------------ synthetic inputs -- */
+
+/* Seeded benchmark inputs, the same generator as the product library's
+ * gdn_b200_fill_synthetic (so the CPU baseline never needs that library):
+ * a SplitMix64 counter keyed by (seed, tensor id) gives two 53-bit uniforms
+ * per element; distribution 0 = normal p0 + p1 * N(0,1) (Box-Muller,
+ * cosine branch), 1 = uniform [p0, p1), 2 = log of uniform (p0, p1].
+ * dtype 1 = bf16 (round to nearest even), 2 = f32.  Computed in double with
+ * the C library's sqrt/log/cos and no fused multiply-add (ISO C mode,
+ * -ffp-contract=off), so both builds give the same bits (a CPU test compares
+ * them). */
+static inline uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+ORACLE_EXPORT int32_t gdn_oracle_fill_synthetic(uint64_t seed, uint64_t tensor_id,
+                                                uint64_t count, int32_t distribution,
+                                                float p0, float p1, int32_t out_dtype,
+                                                void* out) {
+  if ((out == NULL && count > 0) || distribution < 0 || distribution > 2 ||
+      (out_dtype != 1 && out_dtype != 2))
+    return 1;
+  const uint64_t key = splitmix64(splitmix64(seed) ^ (tensor_id * 0xD1B54A32D192ED03ull));
+  const double two_pi = 6.283185307179586476925286766559;
+  /* The product evaluates p0 + p1 * sqrt(..) * cos(..) left to right in
+   * double, and (p1 - p0) in float: the same order here. */
+  const double p0d = (double)p0, p1d = (double)p1, span = (double)(float)(p1 - p0);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < (int64_t)count; ++i) {
+    const uint64_t r1 = splitmix64(key + 2 * (uint64_t)i);
+    const uint64_t r2 = splitmix64(key + 2 * (uint64_t)i + 1);
+    const double u1 = ((double)(r1 >> 11) + 1.0) * (1.0 / 9007199254740992.0);
+    const double u2 = (double)(r2 >> 11) * (1.0 / 9007199254740992.0);
+    double val;
+    if (distribution == 0) {
+      const double scaled = p1d * sqrt(-2.0 * log(u1));
+      val = p0d + scaled * cos(two_pi * u2);
+    } else if (distribution == 1) {
+      val = p0d + span * u2;
+    } else {
+      val = log(p0d + span * u1);
+    }
+    if (out_dtype == 1)
+      ((uint16_t*)out)[i] = f32_to_bf16((float)val);
+    else
+      ((float*)out)[i] = (float)val;
+  }
+  return 0;
+}

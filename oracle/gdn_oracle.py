@@ -59,6 +59,10 @@ def lib():
                                        i32, i32, ctypes.c_void_p, ctypes.c_void_p]
         L.gdn_oracle_threads.restype = i32
         L.gdn_oracle_causal_conv1d.argtypes = [_u16p, _u16p, _u16p, _i32p, i32, i64, i32, _u16p]
+        L.gdn_oracle_fill_synthetic.argtypes = [ctypes.c_uint64, ctypes.c_uint64,
+                                                ctypes.c_uint64, i32, f32, f32, i32,
+                                                ctypes.c_void_p]
+        L.gdn_oracle_fill_synthetic.restype = i32
         _lib = L
     return _lib
 
@@ -76,6 +80,21 @@ def f32_to_bf16(x: np.ndarray) -> np.ndarray:
 
 def bf16_to_f32(h: np.ndarray) -> np.ndarray:
     return (np.ascontiguousarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ------------------------------------------------------ synthetic inputs --
+
+def fill(seed: int, tensor_id: int, shape, distribution: int, p0: float, p1: float,
+         dtype: int) -> np.ndarray:
+    """Seeded host tensor from the oracle's copy of the benchmark generator
+    (bf16 as uint16 bit patterns when dtype is 1, float32 when 2); the same
+    arguments and bits as ``gdn_b200.fill``, without the product library."""
+    n = int(np.prod(shape)) if len(shape) else 1
+    out = np.empty(n, dtype=np.uint16 if dtype == 1 else np.float32)
+    if lib().gdn_oracle_fill_synthetic(seed, tensor_id, n, distribution, p0, p1, dtype,
+                                       out.ctypes.data_as(ctypes.c_void_p)) != 0:
+        raise ValueError("bad distribution or dtype")
+    return out.reshape(shape)
 
 
 # ------------------------------------------------------------ operators --

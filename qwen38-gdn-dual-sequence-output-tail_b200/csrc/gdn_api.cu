@@ -1,6 +1,7 @@
 // C-ABI entry points of include/gdn_b200.h: argument validation, workspace
 // carving and kernel launches.  Host code only; kernels live in
 // gdn_decode.cu, gdn_tail.cu and gdn_chunk.cu.
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -59,24 +60,45 @@ int32_t check_seqlens(const int32_t* cu, int32_t num_seqs, gdn::ChunkTable* tab)
 
 }  // namespace
 
+namespace gdn {
+
+int32_t api_fail(int32_t status, const std::string& message) { return fail(status, message); }
+
+int32_t api_ok() { return ok(); }
+
+namespace {
+std::atomic<uint64_t> g_kernel_launches{0};
+}  // namespace
+
+void note_launches(int n) { g_kernel_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+
+int32_t read_error_word(const void* word_address, cudaStream_t stream) {
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_status(e, "cudaStreamSynchronize");
+  uint32_t word = 0;
+  e = cudaMemcpy(&word, word_address, sizeof(word), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemcpy(error word)");
+  if (word == kErrNone) return ok();
+  const char* what = word == kErrWaitTimeout  ? "a kernel wait ran out of time"
+                     : word == kErrTmemAlloc  ? "TMEM allocation failed"
+                     : word == kErrMisaligned ? "a state row address is not 16-byte aligned"
+                                              : "kernel reported a geometry error";
+  return fail(STATECENTRIC_QWEN38_INTERNAL, std::string("device error: ") + what);
+}
+
+}  // namespace gdn
+
 extern "C" {
 
 const char* gdn_b200_last_error(void) { return g_last_error.c_str(); }
 
+uint64_t gdn_b200_kernel_launches(void) {
+  return gdn::g_kernel_launches.load(std::memory_order_relaxed);
+}
+
 int32_t gdn_b200_workspace_status(const void* workspace, void* stream) {
   if (workspace == nullptr) return fail(STATECENTRIC_QWEN38_INVALID_ARGUMENT, "workspace is null");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return cuda_status(e, "cudaStreamSynchronize");
-  uint32_t word = 0;
-  e = cudaMemcpy(&word, workspace, sizeof(word), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_status(e, "cudaMemcpy(error word)");
-  if (word == gdn::kErrNone) return ok();
-  const char* what = word == gdn::kErrWaitTimeout  ? "a kernel wait ran out of time"
-                     : word == gdn::kErrTmemAlloc  ? "TMEM allocation failed"
-                     : word == gdn::kErrMisaligned ? "a state row address is not 16-byte aligned"
-                                                   : "kernel reported a geometry error";
-  return fail(STATECENTRIC_QWEN38_INTERNAL, std::string("device error: ") + what);
+  return gdn::read_error_word(workspace, static_cast<cudaStream_t>(stream));
 }
 
 // ------------------------------------------------------------- tail ----

@@ -1078,6 +1078,7 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
       tab, tq, tk, a, b, A_log, dt_bias, kq_records, records, qk_heads, value_heads, err);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  note_launches();
 
   const uint32_t st_smem = StateSmemLayout::kTotal;
   e = cudaFuncSetAttribute(gdn_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1088,7 +1089,9 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
   if (!make_tmap_thd(&to, o_out, tokens, value_heads)) return cudaErrorInvalidValue;
   gdn_chunk_state_kernel<<<sgrid, kStateThreads, st_smem, stream>>>(
       tab, tv, to, kq_records, records, state, o_out, qk_heads, value_heads, err);
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (e == cudaSuccess) note_launches();
+  return e;
 }
 
 }  // namespace gdn

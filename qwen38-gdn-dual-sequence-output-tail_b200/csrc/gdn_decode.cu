@@ -310,7 +310,9 @@ cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* 
   gdn_decode_kernel<<<grid, kDecodeThreads, smem, stream>>>(
       q, k, v, a, b, A_log, dt_bias, state, o_out, z, gamma, gated_out, state_rows, units,
       qk_heads, value_heads, static_cast<const uint8_t*>(l2_prefetch), l2_prefetch_bytes, err);
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (e == cudaSuccess) note_launches();
+  return e;
 }
 
 }  // namespace gdn

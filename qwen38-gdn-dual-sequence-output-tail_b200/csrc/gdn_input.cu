@@ -224,6 +224,7 @@ cudaError_t launch_input_side(const ChunkTable& tab, const uint16_t* x, const ui
                                                         q, k, v, qk_dim, v_dim);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    note_launches();
   }
   // The state of every sequence (an empty one keeps its history, or zeros
   // when the call has no context), after the conv has read the old state.
@@ -231,11 +232,14 @@ cudaError_t launch_input_side(const ChunkTable& tab, const uint16_t* x, const ui
   conv_state_update_kernel<<<sgrid, 128, 0, stream>>>(tab, qkv, conv_state, use_state, channels);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  note_launches();
   const int64_t n = tokens * value_heads;
   if (n == 0) return cudaSuccess;
   split_gates_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
       ab, a, b, tokens, value_heads, n_ab);
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (e == cudaSuccess) note_launches();
+  return e;
 }
 
 }  // namespace gdn

@@ -4,7 +4,19 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace gdn {
+
+// Status reporting shared by every C-ABI entry point: api_fail records the
+// message that gdn_b200_last_error() returns on this thread, api_ok clears it.
+int32_t api_fail(int32_t status, const std::string& message);
+int32_t api_ok();
+// Synchronises `stream`, then reads the device error word at `word_address`
+// and turns it into a status (OK, or INTERNAL with the reason).
+int32_t read_error_word(const void* word_address, cudaStream_t stream);
+// Counts kernel launches made by this library (gdn_b200_kernel_launches()).
+void note_launches(int n = 1);
 
 constexpr int kMaxSeqsInternal = 1024;
 

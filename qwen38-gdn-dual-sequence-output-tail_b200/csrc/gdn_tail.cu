@@ -605,7 +605,9 @@ cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uin
     tail_prologue_kernel<1><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(o, z, gamma, gated,
                                                                              pairs, eps);
   }
-  return cudaGetLastError();
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) note_launches();
+  return e;
 }
 
 template <int BN>
@@ -619,7 +621,9 @@ static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, 
   tail_gemm_kernel<BN><<<p.grid, kGemmThreads, smem, stream>>>(
       ta, tb, out, ws, static_cast<int>(M), N, p.tiles_m, p.tiles_n, p.splits, p.kblocks_total,
       p.kblocks_per_split, err);
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (e == cudaSuccess) note_launches();
+  return e;
 }
 
 // out[M, N] = a[M, K] @ w[N, K]^T  (bf16 in, f32 accumulate, bf16 out).
@@ -651,9 +655,11 @@ cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = overlap_previous ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, tail_gemm_cluster_kernel<kClusterBN, kClusterStages>, ta, tb,
-                              out, static_cast<int>(M), N, p.kblocks_total, p.kblocks_per_split,
-                              overlap_previous ? 1 : 0, err);
+    ec = cudaLaunchKernelEx(&cfg, tail_gemm_cluster_kernel<kClusterBN, kClusterStages>, ta, tb,
+                            out, static_cast<int>(M), N, p.kblocks_total, p.kblocks_per_split,
+                            overlap_previous ? 1 : 0, err);
+    if (ec == cudaSuccess) note_launches();
+    return ec;
   }
   cudaError_t e = (p.bn == 256)   ? launch_gemm_bn<256>(ta, tb, out, ws, M, N, p, err, stream)
                   : (p.bn == 128) ? launch_gemm_bn<128>(ta, tb, out, ws, M, N, p, err, stream)
@@ -664,6 +670,7 @@ cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out
     splitk_reduce_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(ws, out, n4,
                                                                                    p.splits);
     e = cudaGetLastError();
+    if (e == cudaSuccess) note_launches();
   }
   return e;
 }

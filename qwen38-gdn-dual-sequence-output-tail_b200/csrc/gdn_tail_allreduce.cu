@@ -355,7 +355,9 @@ cudaError_t launch_ar(const CUtensorMap& ta, const CUtensorMap& tb, const TailPe
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   tail_gemm_allreduce_kernel<W><<<grid, kArThreads, smem, stream>>>(ta, tb, peers, p, err);
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (e == cudaSuccess) note_launches();
+  return e;
 }
 
 }  // namespace

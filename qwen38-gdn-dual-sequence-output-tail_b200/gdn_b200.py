@@ -37,6 +37,7 @@ ABI_MISMATCH = 6
 # Every exported symbol of include/gdn_b200.h and the provider header.
 EXPORTED_SYMBOLS = (
     "gdn_b200_last_error",
+    "gdn_b200_kernel_launches",
     "gdn_b200_workspace_status",
     "gdn_b200_output_tail_workspace_bytes",
     "gdn_b200_output_tail",
@@ -60,6 +61,8 @@ EXPORTED_SYMBOLS = (
     "gdn_b200_exchange_close",
     "gdn_b200_output_tail_allreduce_workspace_bytes",
     "gdn_b200_output_tail_allreduce",
+    "gdn_b200_output_tail_no_alloc",
+    "gdn_b200_output_tail_no_alloc_status",
     "statecentric_qwen38_provider_query_v1",
 )
 
@@ -85,6 +88,7 @@ def lib() -> ctypes.CDLL:
                                   ctypes.c_uint64, ctypes.c_float)
         i32p = ctypes.POINTER(ctypes.c_int32)
         L.gdn_b200_last_error.restype = ctypes.c_char_p
+        L.gdn_b200_kernel_launches.restype = u64
         L.gdn_b200_workspace_status.argtypes = [vp, vp]
         L.gdn_b200_workspace_status.restype = i32
         L.gdn_b200_output_tail_workspace_bytes.argtypes = [i64, i32, i32]
@@ -134,12 +138,21 @@ def lib() -> ctypes.CDLL:
                                                      ctypes.POINTER(TailGroupV1), ctypes.c_uint32,
                                                      vp, u64, vp]
         L.gdn_b200_output_tail_allreduce.restype = i32
+        L.gdn_b200_output_tail_no_alloc.argtypes = [vp] * 5 + [i64, i32, i32, f32, vp]
+        L.gdn_b200_output_tail_no_alloc.restype = i32
+        L.gdn_b200_output_tail_no_alloc_status.argtypes = [vp]
+        L.gdn_b200_output_tail_no_alloc_status.restype = i32
         _lib = L
     return _lib
 
 
 def last_error() -> str:
     return lib().gdn_b200_last_error().decode()
+
+
+def kernel_launches() -> int:
+    """Kernels this library has launched in this process so far."""
+    return int(lib().gdn_b200_kernel_launches())
 
 
 def _check(status: int) -> None:
@@ -187,6 +200,25 @@ def output_tail(o, z, gamma, w_out, out=None, eps=1e-6, workspace=None, stream=N
                                       rows, hv, hidden, eps, _ptr(workspace),
                                       workspace.numel(), _stream(stream)))
     return out
+
+
+def output_tail_no_alloc(o, z, gamma, w_out, out=None, eps=1e-6, stream=None):
+    """The output tail with the library's static scratch instead of a
+    workspace (``gdn_b200_output_tail_no_alloc``): rows <= 128,
+    Hv*128 <= 4096, hidden <= 2048."""
+    import torch
+    rows, hv, hidden = o.shape[0], o.shape[1], w_out.shape[0]
+    if out is None:
+        out = torch.empty(rows, hidden, dtype=torch.bfloat16, device=o.device)
+    _check(lib().gdn_b200_output_tail_no_alloc(_ptr(o), _ptr(z), _ptr(gamma), _ptr(w_out),
+                                               _ptr(out), rows, hv, hidden, eps,
+                                               _stream(stream)))
+    return out
+
+
+def output_tail_no_alloc_status(stream=None) -> None:
+    """Synchronises and raises if the last no-alloc tail recorded a device error."""
+    _check(lib().gdn_b200_output_tail_no_alloc_status(_stream(stream)))
 
 
 def decode_step(q, k, v, a, b, A_log, dt_bias, state, o_out=None, z=None, gamma=None,
@@ -497,12 +529,13 @@ TID = dict(q=1, k=2, v=3, a=4, b=5, z=6, A_log=7, dt_bias=8, gamma=9, w_out=10, 
 
 
 def synthetic_layer_inputs(cu_seqlens, geom: Geometry, seed: int = 0, state_std: float = 0.0,
-                           a_log_hi: float = 16.0, shard=None):
+                           a_log_hi: float = 16.0, shard=None, fill=fill):
     """Host inputs with the benchmark distributions: q, k, v, z ~ N(0,1);
     a ~ N(0,1); dt_bias ~ N(0,0.1); A_log = log U(0, a_log_hi); b ~ N(0,1);
     gamma = 1 + N(0, 0.02); w_out ~ N(0, 0.02); state ~ N(0, state_std) (zero
     when state_std is 0).  ``shard = (rank, world)`` slices the head-parallel
-    shard of rank ``rank`` out of the full-geometry tensors."""
+    shard of rank ``rank`` out of the full-geometry tensors.  ``fill`` is the
+    generator (this module's, or any function with its signature and bits)."""
     cu = np.asarray(cu_seqlens, dtype=np.int64)
     T = int(cu[-1])
     S = len(cu) - 1

@@ -197,3 +197,25 @@ def test_causal_conv_continuation_is_exact():
              for i, j in ((0, 2), (2, 3), (3, 29), (29, 50))]
     assert np.array_equal(whole, np.concatenate(parts))
     assert np.array_equal(st_a, st_b)
+
+
+@pytest.mark.parametrize("dist,p0,p1", [(G.NORMAL, 0.0, 1.0), (G.NORMAL, 1.0, 0.02),
+                                        (G.NORMAL, 0.0, 0.05), (G.UNIFORM, -2.0, 3.0),
+                                        (G.LOG_UNIFORM, 0.0, 16.0)])
+@pytest.mark.parametrize("dtype", [G.BF16, G.F32])
+def test_oracle_generator_matches_product_generator(dist, p0, p1, dtype):
+    # The CPU baseline builds its inputs with the oracle's generator so that
+    # it never loads the product library; both must give the same bits.
+    a = G.fill(3, 11, (65537,), dist, p0, p1, dtype)
+    b = O.fill(3, 11, (65537,), dist, p0, p1, dtype)
+    assert np.array_equal(a.view(np.uint8), b.view(np.uint8))
+
+
+def test_benchmark_inputs_from_the_oracle_generator_are_identical():
+    cu = np.array([0, 70, 200], np.int32)
+    geom = G.Geometry(4, 8, 256)
+    a = G.synthetic_layer_inputs(cu, geom, seed=1, state_std=0.05)
+    b = G.synthetic_layer_inputs(cu, geom, seed=1, state_std=0.05, fill=O.fill)
+    assert a.keys() == b.keys()
+    for name in a:
+        assert np.array_equal(a[name].view(np.uint8), b[name].view(np.uint8)), name
