@@ -58,8 +58,11 @@ enum {
 
 /* Execution flags (P:2259-2303).  The reference admits GDN_FORWARD_V1 alone
  * or together with exactly one of the PREFILL_* variants; all of those start
- * from the hidden state x and need the input projections and causal conv,
- * which this build does not contain (Submit answers UNSUPPORTED).
+ * from the hidden state x (inputs x, w_qkv, w_z, w_a, w_b, conv_w, A_log,
+ * dt_bias, gamma, w_out; states gdn.conv then gdn.recurrent) and are executed
+ * here: projections, causal conv + SiLU and the q/k/v split run on the device
+ * before the layer (the PREFILL_* variants only change how the reference
+ * splits q/k/v, so all of them run the same kernels).
  * B200: GDN_FORWARD_V1 | GDN_POST_PROJECTION_V6 starts from the projected
  * q, k, v, a, b, z (the reference's precomputed-projection form, P:230-247);
  * GDN_FORWARD_V1 | GDN_OUTPUT_TAIL_V7 runs only the gated-RMSNorm + out_proj

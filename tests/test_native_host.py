@@ -87,3 +87,34 @@ def test_library_exports_every_declared_symbol():
 def test_graph_binding_rules(tmp_path):
     r = _build_and_run(tmp_path, "graph_binding_test.cpp")
     assert r.returncode == 0, f"graph binding test failed with code {r.returncode}"
+
+
+def test_plans_and_graph_binding_match_the_reference_headers(tmp_path):
+    """Bit-exact agreement with the reference's own admission and binding code.
+
+    ``oracle/plan_probe.cpp`` is compiled against the reference's headers
+    where they lie (qwen38_gdn_dual_sequence_tail_policy.h,
+    qwen38_gdn_geometry_policy.h and qwen38_gdn_graph_binding.h, the last one
+    against this repository's reconstructed provider ABI header, which must
+    therefore provide every field it reads) into ``oracle/_ref/``, and against
+    ``gdn_plan.h`` / ``gdn_graph_binding.h``.  Both print every feature
+    predicate over all flag combinations, the chunk-vs-recurrent rule, every
+    plan over all gates x token-count vectors of length 0-4 (admitted cases
+    listed, every answer hashed) and 20000 COPY-binding cases (refusal message
+    or the full copy sequence); the outputs must be identical."""
+    oracle = os.path.join(ROOT, "oracle")
+    ref_bin = os.path.join(oracle, "_ref", "plan_probe_ref")
+    if os.path.isdir("/root/reference/native/include"):
+        subprocess.run(["make", "-s", "-C", oracle, "ref"], check=True)
+    if not os.path.exists(ref_bin):
+        pytest.skip("the reference headers are not present and oracle/_ref was not built")
+    repo_bin = str(tmp_path / "plan_probe_repo")
+    subprocess.run(["make", "-s", "-C", oracle, "probe", f"PROBE_OUT={repo_bin}"], check=True)
+    ref = subprocess.run([ref_bin], capture_output=True, text=True, check=True).stdout
+    ours = subprocess.run([repo_bin], capture_output=True, text=True, check=True).stdout
+    assert ref.count("\n") > 20000
+    assert "admitted=8" in ref
+    ref_lines, our_lines = ref.splitlines(), ours.splitlines()
+    assert len(ref_lines) == len(our_lines)
+    diff = [(a, b) for a, b in zip(ref_lines, our_lines) if a != b]
+    assert not diff, diff[:5]
