@@ -133,6 +133,44 @@ __device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, u
   lo = pack_bf16x2(x0 - bf16lo_f32(hi), x1 - bf16hi_f32(hi));
 }
 
+// ------------------------------------------------- output-tail gating -----
+// The output tail's gate for eight elements of one (row, head) pair, the
+// reference's RmsNorm -> Silu -> Mul operator chain with a bf16 rounding at
+// each operator boundary (P:1443-1497):
+//   gated = bf16( bf16(o * rstd * gamma) * bf16(SiLU(z)) ).
+// Sixteen consecutive lanes hold the 128 elements of a pair (8 each):
+// gate_sumsq16 returns the pair's sum of o^2 in every one of those lanes.
+__device__ __forceinline__ float gate_sumsq16(const uint32_t (&ow)[4]) {
+  float ss = 0.f;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float x0 = bf16lo_f32(ow[p]), x1 = bf16hi_f32(ow[p]);
+    ss += x0 * x0 + x1 * x1;
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  return ss;
+}
+__device__ __forceinline__ uint4 gate8(const uint32_t (&ow)[4], const uint32_t (&zw)[4],
+                                       const uint32_t (&gw)[4], float rstd) {
+  uint32_t res[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    float r2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float x = e ? bf16hi_f32(ow[p]) : bf16lo_f32(ow[p]);
+      const float zz = e ? bf16hi_f32(zw[p]) : bf16lo_f32(zw[p]);
+      const float gg = e ? bf16hi_f32(gw[p]) : bf16lo_f32(gw[p]);
+      const float nrm = round_bf16(x * rstd * gg);
+      const float sl = round_bf16(__fdividef(zz, 1.0f + __expf(-zz)));
+      r2[e] = nrm * sl;
+    }
+    res[p] = pack_bf16x2(r2[0], r2[1]);
+  }
+  return make_uint4(res[0], res[1], res[2], res[3]);
+}
+
 // Packed f32x2 arithmetic (one instruction for two IEEE fp32 lanes).
 __device__ __forceinline__ unsigned long long f2_pack(float2 v) {
   unsigned long long r;
@@ -261,6 +299,12 @@ __device__ __forceinline__ void bulk_commit() {
 template <int N>
 __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N of this thread's committed bulk groups are still
+// incomplete (their writes not yet performed).
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 // Waits until every committed bulk group of this thread has completed.
 __device__ __forceinline__ void bulk_wait_all() {

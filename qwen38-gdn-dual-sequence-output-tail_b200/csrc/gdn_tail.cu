@@ -63,32 +63,9 @@ tail_prologue_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict_
   for (int i = 0; i < kProloguePairs; ++i) {
     const uint32_t ow[4] = {ov[i].x, ov[i].y, ov[i].z, ov[i].w};
     const uint32_t zw[4] = {zv[i].x, zv[i].y, zv[i].z, zv[i].w};
-    float ss = 0.f;
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const float x0 = bf16lo_f32(ow[p]), x1 = bf16hi_f32(ow[p]);
-      ss += x0 * x0 + x1 * x1;
-    }
-#pragma unroll
-    for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    const float rstd = rsqrtf(ss * (1.0f / 128.0f) + eps);
-    uint32_t res[4];
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      float r2[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float x = e ? bf16hi_f32(ow[p]) : bf16lo_f32(ow[p]);
-        const float zz = e ? bf16hi_f32(zw[p]) : bf16lo_f32(zw[p]);
-        const float gg = e ? bf16hi_f32(gw[p]) : bf16lo_f32(gw[p]);
-        const float nrm = round_bf16(x * rstd * gg);
-        const float sl = round_bf16(__fdividef(zz, 1.0f + __expf(-zz)));
-        r2[e] = nrm * sl;
-      }
-      res[p] = pack_bf16x2(r2[0], r2[1]);
-    }
-    if (live[i])
-      *reinterpret_cast<uint4*>(gated + base[i]) = make_uint4(res[0], res[1], res[2], res[3]);
+    const float rstd = rsqrtf(gate_sumsq16(ow) * (1.0f / 128.0f) + eps);
+    const uint4 res = gate8(ow, zw, gw, rstd);
+    if (live[i]) *reinterpret_cast<uint4*>(gated + base[i]) = res;
   }
 }
 
