@@ -162,19 +162,26 @@ def use_fused_reduce(world: int, reduce: str) -> bool:
     return world > 1 and (reduce == "fused" or (reduce == "auto" and world == 2))
 
 
+def reduce_desc(world: int, reduce: str) -> str:
+    if world == 1:
+        return ""
+    if use_fused_reduce(world, reduce):
+        return " + rank sum fused into the tail GEMM (NVLink peer memory)"
+    if reduce == "rs":
+        return (" + nccl reduce-scatter (each rank receives its row shard), overlapping the "
+                "next step on a communication stream")
+    return " + nccl all-reduce, overlapping the next step on a communication stream"
+
+
 def prefill_config(world: int, reduce: str) -> dict:
     """The headline workload's config, the same for both arms."""
     nseq = SEQS_PER_GPU * world
     T = nseq * SEQ_LEN
     hk, hv = QK_HEADS // world, V_HEADS // world
     qkvz_mb = (2 * T * hk * 128 + 2 * T * hv * 128) * 2 / 1e6
-    fused = use_fused_reduce(world, reduce)
     return {"workload": workload_desc(nseq), "tokens_per_step": T, "sequences": nseq,
             "seq_len": SEQ_LEN,
-            "parallelism": f"head-parallel tp{world}" + (
-                "" if world == 1 else
-                " + rank sum fused into the tail GEMM (NVLink peer memory)" if fused
-                else " + nccl all-reduce"),
+            "parallelism": f"head-parallel tp{world}" + reduce_desc(world, reduce),
             "l2": "inputs larger than L2 (q,k,v,z = %.0f MB per step)" % qkvz_mb}
 
 
@@ -358,11 +365,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--component-iters", type=int, default=50,
                     help="calls timed per small-shape component (N=1 only)")
-    ap.add_argument("--reduce", choices=["auto", "fused", "nccl"], default="auto",
-                    help="N > 1: rank sum fused into the tail GEMM over NVLink peer memory, "
-                         "or the unfused tail + a bf16 NCCL all-reduce; auto = fused for 2 "
-                         "GPUs, NCCL from 4 (measured: 2 GPUs 0.523 vs 0.587 ms per step, "
-                         "4 GPUs 0.904 vs 0.809)")
+    ap.add_argument("--reduce", choices=["auto", "fused", "nccl", "rs"], default="auto",
+                    help="N > 1: rank sum fused into the tail GEMM over NVLink peer memory "
+                         "(fused), a bf16 NCCL all-reduce (nccl) or reduce-scatter (rs: each "
+                         "rank receives its row shard) overlapping the next step; auto = "
+                         "fused for 2 GPUs, nccl from 4")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
@@ -425,29 +432,54 @@ def main():
         ws_ar = torch.empty(G.output_tail_allreduce_workspace_bytes(T, hv), dtype=torch.uint8,
                             device=dev)
 
-    def step():
+    # NCCL reductions run on their own stream: the reduction of step i's
+    # rank-partial output overlaps step i + 1, which depends only on the
+    # recurrent state (two output buffers; step i + 2 reuses step i's buffer
+    # once its reduction is done).
+    comm = torch.cuda.Stream(device=dev) if world > 1 and not fused else None
+    red_outs = [out, torch.empty_like(out)] if comm is not None else [out]
+    red_shards = ([torch.empty(T // world, HIDDEN, dtype=torch.bfloat16, device=dev)
+               for _ in range(2)] if args.reduce == "rs" and comm is not None else None)
+    ev_red_in = [torch.cuda.Event() for _ in range(2)]
+    ev_red = [torch.cuda.Event() for _ in range(2)]
+    red_used = [False, False]
+
+    def step(i=0):
         if fused:
             G.chunk_prefill(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"], t["dt_bias"],
                             t["state"], cu, o_out=o_buf, workspace=ws_chunk, stream=stream)
             group.output_tail(o_buf, t["z"], t["gamma"], t["w_out"], workspace=ws_ar,
                               stream=stream)
             return
+        b = i & 1 if comm is not None else 0
+        if comm is not None and red_used[b]:
+            stream.wait_event(ev_red[b])           # step i - 2's reduction has read it
         G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
-                        t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu, out=out,
+                        t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu, out=red_outs[b],
                         workspace=ws, stream=stream)
-        if world > 1:
-            dist.all_reduce(out)
+        if comm is not None:
+            ev_red_in[b].record(stream)
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev_red_in[b])
+                if red_shards is not None:
+                    dist.reduce_scatter_tensor(red_shards[b], red_outs[b])
+                else:
+                    dist.all_reduce(red_outs[b])
+                ev_red[b].record(comm)
+            red_used[b] = True
 
     def timed(fn, iters, warm):
-        for _ in range(warm):
-            fn()
+        for i in range(warm):
+            fn(i)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
-        for _ in range(iters):
-            fn()
+        for i in range(iters):
+            fn(i)
+        if comm is not None and fn is step:
+            stream.wait_stream(comm)                # the last reduction is inside the region
         e.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -459,8 +491,8 @@ def main():
             ms = float(v.item())
         return ms
 
-    for _ in range(args.warmup):
-        step()
+    for i in range(args.warmup):
+        step(i)
     torch.cuda.synchronize()
     G.workspace_status(ws_ar if fused else ws, stream)
     launches0 = G.kernel_launches()
@@ -478,16 +510,16 @@ def main():
                           device=dev)
     ws_tail = torch.empty(G.output_tail_workspace_bytes(T, hv, HIDDEN), dtype=torch.uint8,
                           device=dev)
-    core_ms = timed(lambda: G.chunk_prefill(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"],
+    core_ms = timed(lambda i=0: G.chunk_prefill(t["q"], t["k"], t["v"], t["a"], t["b"], t["A_log"],
                                             t["dt_bias"], t["state"], cu, o_out=o,
                                             workspace=ws_core, stream=stream), args.steps, 2)
     if fused:
         # the tail with the rank sum fused in (what the step runs)
-        tail_ms = timed(lambda: group.output_tail(o, t["z"], t["gamma"], t["w_out"],
+        tail_ms = timed(lambda i=0: group.output_tail(o, t["z"], t["gamma"], t["w_out"],
                                                   workspace=ws_ar, stream=stream), args.steps, 2)
         G.workspace_status(ws_ar, stream)
     else:
-        tail_ms = timed(lambda: G.output_tail(o, t["z"], t["gamma"], t["w_out"], out=out,
+        tail_ms = timed(lambda i=0: G.output_tail(o, t["z"], t["gamma"], t["w_out"], out=out,
                                               workspace=ws_tail, stream=stream), args.steps, 2)
     # The input side (x -> projections -> causal conv + SiLU -> q/k/v split,
     # conv-state update) on the same tokens, timed alone: the layer from x
@@ -498,7 +530,7 @@ def main():
                         device=dev)
     in_out = (torch.empty_like(t["q"]), torch.empty_like(t["k"]), torch.empty_like(t["v"]),
               torch.empty_like(t["z"]), torch.empty_like(t["a"]), torch.empty_like(t["b"]))
-    in_ms = timed(lambda: G.input_side(xs["x"], xs["w_qkv"], xs["w_z"], xs["w_a"], xs["w_b"],
+    in_ms = timed(lambda i=0: G.input_side(xs["x"], xs["w_qkv"], xs["w_z"], xs["w_a"], xs["w_b"],
                                        xs["conv_w"], xs["conv_state"], cu, hk, out=in_out,
                                        workspace=ws_in, stream=stream), args.steps, 2)
     G.workspace_status(ws_in, stream)
@@ -551,6 +583,8 @@ def main():
     for n in host:
         t_in[1][n] = torch.empty_like(t[n])
     outs = [out, torch.empty_like(out)]
+    e2e_shards = [torch.empty(T // world, HIDDEN, dtype=torch.bfloat16, device=dev)
+                  for _ in range(2)]
     s_in = torch.cuda.Stream(device=dev)
     s_out = torch.cuda.Stream(device=dev)
     ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -570,12 +604,15 @@ def main():
         if i >= 2:
             stream.wait_event(ev_out[b])        # step i - 2's output has been read back
         pending.append(prov.submit_layer(t_in[b], t["state"], outs[b], cu, stream=stream))
-        if world > 1:
+        if world > 1 and args.reduce == "rs":
+            dist.reduce_scatter_tensor(e2e_shards[b], outs[b])
+        elif world > 1:
             dist.all_reduce(outs[b])
         ev_comp[b].record(stream)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_comp[b])
-            host_outs[b].copy_(outs[b][r0:r1], non_blocking=True)
+            host_outs[b].copy_(e2e_shards[b] if world > 1 and args.reduce == "rs"
+                               else outs[b][r0:r1], non_blocking=True)
             ev_out[b].record(s_out)
         while len(pending) > 1:                 # keep one submission in flight
             ev = pending.pop(0)
