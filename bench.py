@@ -159,7 +159,11 @@ def workload_desc(nseq: int) -> str:
 
 
 def use_fused_reduce(world: int, reduce: str) -> bool:
-    return world > 1 and (reduce == "fused" or (reduce == "auto" and world == 2))
+    return world > 1 and reduce == "fused"
+
+
+def use_ce_reduce(world: int, reduce: str) -> bool:
+    return world > 1 and reduce in ("ce", "auto")
 
 
 def reduce_desc(world: int, reduce: str) -> str:
@@ -167,6 +171,9 @@ def reduce_desc(world: int, reduce: str) -> str:
         return ""
     if use_fused_reduce(world, reduce):
         return " + rank sum fused into the tail GEMM (NVLink peer memory)"
+    if use_ce_reduce(world, reduce):
+        return (" + rank sum as a reduce-scatter over the copy engines (peer copies over "
+                "NVLink, each rank receives its row shard), overlapping the next step")
     if reduce == "rs":
         return (" + nccl reduce-scatter (each rank receives its row shard), overlapping the "
                 "next step on a communication stream")
@@ -365,11 +372,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--component-iters", type=int, default=50,
                     help="calls timed per small-shape component (N=1 only)")
-    ap.add_argument("--reduce", choices=["auto", "fused", "nccl", "rs"], default="auto",
-                    help="N > 1: rank sum fused into the tail GEMM over NVLink peer memory "
-                         "(fused), a bf16 NCCL all-reduce (nccl) or reduce-scatter (rs: each "
-                         "rank receives its row shard) overlapping the next step; auto = "
-                         "fused for 2 GPUs, nccl from 4")
+    ap.add_argument("--reduce", choices=["auto", "ce", "fused", "nccl", "rs"], default="auto",
+                    help="N > 1: the rank sum as a copy-engine reduce-scatter overlapping the "
+                         "next step (ce, the default), fused into the tail GEMM over NVLink "
+                         "peer memory (fused), or a bf16 NCCL all-reduce (nccl) or "
+                         "reduce-scatter (rs) on a communication stream")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
@@ -436,6 +443,19 @@ def main():
     # rank-partial output overlaps step i + 1, which depends only on the
     # recurrent state (two output buffers; step i + 2 reuses step i's buffer
     # once its reduction is done).
+    ce = use_ce_reduce(world, args.reduce)
+    rsum = None
+    if ce:
+        def exchange_ce(payload):
+            got = [None] * world
+            dist.all_gather_object(got, payload)
+            return got
+
+        rsum = G.RankSum(T, HIDDEN, rank, world, dev, exchange=exchange_ce)
+        ce_shards = [torch.empty(T // world, HIDDEN, dtype=torch.bfloat16, device=dev)
+                     for _ in range(2)]
+    epoch = [0]
+
     comm = torch.cuda.Stream(device=dev) if world > 1 and not fused else None
     red_outs = [out, torch.empty_like(out)] if comm is not None else [out]
     red_shards = ([torch.empty(T // world, HIDDEN, dtype=torch.bfloat16, device=dev)
@@ -450,6 +470,17 @@ def main():
                             t["state"], cu, o_out=o_buf, workspace=ws_chunk, stream=stream)
             group.output_tail(o_buf, t["z"], t["gamma"], t["w_out"], workspace=ws_ar,
                               stream=stream)
+            return
+        if ce:
+            # The layer writes its rank-partial straight into the exchange
+            # buffer of this epoch; the copy engines move the rows.
+            epoch[0] += 1
+            e = epoch[0]
+            rsum.acquire(e, stream)
+            G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
+                            t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu,
+                            out=rsum.part(e, T), workspace=ws, stream=stream)
+            rsum.reduce(e, T, ce_shards[e & 1], stream, comm)
             return
         b = i & 1 if comm is not None else 0
         if comm is not None and red_used[b]:
@@ -501,6 +532,8 @@ def main():
     launches = G.kernel_launches() - launches0
     clk = clocks.summary()
     G.workspace_status(ws_ar if fused else ws, stream)
+    if rsum is not None:
+        rsum.status(comm)
     value = T / (ms * 1e-3)   # T = every token of the job: ranks hold head shards of the same tokens
 
     # Components, timed alone with CUDA events on the launching stream:
@@ -603,6 +636,23 @@ def main():
         stream.wait_event(ev_in[b])
         if i >= 2:
             stream.wait_event(ev_out[b])        # step i - 2's output has been read back
+        if ce:
+            epoch[0] += 1
+            e = epoch[0]
+            rsum.acquire(e, stream)
+            pending.append(prov.submit_layer(t_in[b], t["state"], rsum.part(e, T), cu,
+                                             stream=stream))
+            rsum.reduce(e, T, e2e_shards[b], stream, comm)
+            ev_comp[b].record(comm)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_comp[b])
+                host_outs[b].copy_(e2e_shards[b], non_blocking=True)
+                ev_out[b].record(s_out)
+            while len(pending) > 1:
+                ev = pending.pop(0)
+                prov.wait(ev)
+                prov.release(ev)
+            return
         pending.append(prov.submit_layer(t_in[b], t["state"], outs[b], cu, stream=stream))
         if world > 1 and args.reduce == "rs":
             dist.reduce_scatter_tensor(e2e_shards[b], outs[b])
@@ -673,6 +723,8 @@ def main():
         dist.barrier()
         if group is not None:
             group.close()
+        if rsum is not None:
+            rsum.close()
         dist.destroy_process_group()
 
 

@@ -283,6 +283,43 @@ GDN_B200_API int32_t gdn_b200_exchange_free(void* region);
 GDN_B200_API int32_t gdn_b200_exchange_export(const void* region, void* handle);
 GDN_B200_API int32_t gdn_b200_exchange_open(const void* handle, void** region);
 GDN_B200_API int32_t gdn_b200_exchange_close(void* region);
+/* Rank sum of the head-parallel layer's rank-partial outputs over the copy
+ * engines: a reduce-scatter.  No counterpart in the reference, which returns
+ * the rank-partial (P:3541-3547) and leaves the sum to its engine; this is
+ * the B200 form of that engine step.  Every rank ends with its row shard
+ *   shard_r = bf16( sum over ranks q, in rank order, in f32, of
+ *                   partial_q[rows r*rows/W .. (r+1)*rows/W) )
+ * (W = world_size); the rows move as cudaMemcpyAsync peer copies, i.e. on the
+ * copy engines over NVLink, so no SM takes part in the transfer and it
+ * overlaps the next layer step.  A consumer that needs every row on every
+ * rank gathers the shards afterwards.
+ *
+ * Each rank owns a region of gdn_b200_rank_sum_bytes bytes
+ * (gdn_b200_exchange_alloc: zero-filled), exported and opened like the fused
+ * tail's regions and listed by rank in a gdn_b200_tail_group_v1 (max_rows a
+ * multiple of world_size, hidden a multiple of 8).  Per epoch (1, 2, 3 ...,
+ * the same on every rank):
+ *   gdn_b200_rank_sum_acquire(group, e, err, stream)   before the layer
+ *   the layer writes its [rows, hidden] bf16 rank-partial to
+ *       gdn_b200_rank_sum_part(group, e) on `stream`
+ *   gdn_b200_rank_sum(group, e, rows, shard_out, err, stream, comm_stream)
+ * Acquire waits (on `stream`) until every rank has copied out this rank's
+ * part of epoch e - 2, whose buffer the layer of epoch e reuses.  The sum
+ * publishes the part (on `stream`), then on `comm_stream` waits for every
+ * rank's part of epoch e, copies this rank's rows of each, tells every rank
+ * they are out, and writes shard_out [rows / world_size, hidden] bf16.
+ * Waits are bounded (2 s): a rank that does not take part leaves
+ * kErrWaitTimeout in *err (a device word, read with
+ * gdn_b200_workspace_status). */
+GDN_B200_API uint64_t gdn_b200_rank_sum_bytes(int64_t max_rows, int32_t hidden,
+                                              int32_t world_size);
+GDN_B200_API void* gdn_b200_rank_sum_part(const gdn_b200_tail_group_v1* group, uint32_t epoch);
+GDN_B200_API int32_t gdn_b200_rank_sum_acquire(const gdn_b200_tail_group_v1* group,
+                                               uint32_t epoch, uint32_t* err, void* stream);
+GDN_B200_API int32_t gdn_b200_rank_sum(const gdn_b200_tail_group_v1* group, uint32_t epoch,
+                                       int64_t rows, void* shard_out, uint32_t* err,
+                                       void* stream, void* comm_stream);
+
 GDN_B200_API uint64_t gdn_b200_output_tail_allreduce_workspace_bytes(int64_t rows,
                                                                      int32_t value_heads);
 GDN_B200_API int32_t gdn_b200_output_tail_allreduce(const void* o, const void* z,

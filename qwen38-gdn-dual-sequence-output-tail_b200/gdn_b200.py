@@ -61,6 +61,10 @@ EXPORTED_SYMBOLS = (
     "gdn_b200_exchange_close",
     "gdn_b200_output_tail_allreduce_workspace_bytes",
     "gdn_b200_output_tail_allreduce",
+    "gdn_b200_rank_sum_bytes",
+    "gdn_b200_rank_sum_part",
+    "gdn_b200_rank_sum_acquire",
+    "gdn_b200_rank_sum",
     "gdn_b200_output_tail_no_alloc",
     "gdn_b200_output_tail_no_alloc_status",
     "statecentric_qwen38_provider_query_v1",
@@ -138,6 +142,16 @@ def lib() -> ctypes.CDLL:
                                                      ctypes.POINTER(TailGroupV1), ctypes.c_uint32,
                                                      vp, u64, vp]
         L.gdn_b200_output_tail_allreduce.restype = i32
+        L.gdn_b200_rank_sum_bytes.argtypes = [i64, i32, i32]
+        L.gdn_b200_rank_sum_bytes.restype = u64
+        L.gdn_b200_rank_sum_part.argtypes = [ctypes.POINTER(TailGroupV1), ctypes.c_uint32]
+        L.gdn_b200_rank_sum_part.restype = vp
+        L.gdn_b200_rank_sum_acquire.argtypes = [ctypes.POINTER(TailGroupV1), ctypes.c_uint32,
+                                                vp, vp]
+        L.gdn_b200_rank_sum_acquire.restype = i32
+        L.gdn_b200_rank_sum.argtypes = [ctypes.POINTER(TailGroupV1), ctypes.c_uint32, i64, vp,
+                                        vp, vp, vp]
+        L.gdn_b200_rank_sum.restype = i32
         L.gdn_b200_output_tail_no_alloc.argtypes = [vp] * 5 + [i64, i32, i32, f32, vp]
         L.gdn_b200_output_tail_no_alloc.restype = i32
         L.gdn_b200_output_tail_no_alloc_status.argtypes = [vp]
@@ -487,6 +501,83 @@ class TailGroup:
         self._opened = []
         if self._own is not None:
             self.out = None
+            lib().gdn_b200_exchange_free(ctypes.c_void_p(self._own))
+            self._own = None
+
+
+class RankSum:
+    """One rank of a copy-engine rank sum (``gdn_b200_rank_sum``): the
+    rank's region (two partial-output buffers, staging, flags), the other
+    ranks' regions mapped into this process, and the epoch.
+
+    Per step: :meth:`part` gives the buffer the layer writes its rank-partial
+    output into; call :meth:`acquire` before the layer and :meth:`reduce`
+    after it, on the layer's stream; the shard is written on ``comm_stream``.
+    ``exchange(payload: bytes) -> list[bytes]`` as for :class:`TailGroup`."""
+
+    def __init__(self, max_rows: int, hidden: int, rank: int, world_size: int, device,
+                 exchange=None):
+        import torch
+        self.device = torch.device(device)
+        self.max_rows, self.hidden = int(max_rows), int(hidden)
+        self.rank, self.world_size = int(rank), int(world_size)
+        nbytes = int(lib().gdn_b200_rank_sum_bytes(max_rows, hidden, world_size))
+        if nbytes == 0:
+            raise GdnError(INVALID_ARGUMENT, "invalid rank-sum geometry")
+        self._opened = []
+        region = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _check(lib().gdn_b200_exchange_alloc(nbytes, ctypes.byref(region)))
+        self._own = region.value
+        regions = [None] * world_size
+        regions[rank] = self._own
+        if world_size > 1:
+            handle = (ctypes.c_uint8 * EXCHANGE_HANDLE_BYTES)()
+            _check(lib().gdn_b200_exchange_export(ctypes.c_void_p(self._own), handle))
+            geometry = struct.pack("<qii", max_rows, hidden, world_size)
+            payloads = exchange(bytes(handle) + geometry)
+            if any(bytes(pl[EXCHANGE_HANDLE_BYTES:]) != geometry for pl in payloads):
+                self.close()
+                raise GdnError(INVALID_ARGUMENT, "ranks disagree on max_rows, hidden or world size")
+            for i, payload in enumerate(payloads):
+                if i == rank:
+                    continue
+                h = (ctypes.c_uint8 * EXCHANGE_HANDLE_BYTES).from_buffer_copy(
+                    bytes(payload[:EXCHANGE_HANDLE_BYTES]))
+                peer = ctypes.c_void_p()
+                with torch.cuda.device(self.device):
+                    _check(lib().gdn_b200_exchange_open(h, ctypes.byref(peer)))
+                regions[i] = peer.value
+                self._opened.append(peer.value)
+        self.group = TailGroupV1(rank, world_size, max_rows, hidden, 0,
+                                 (ctypes.c_void_p * MAX_RANKS)(*regions))
+        self._err = torch.zeros(64, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+
+    def part(self, epoch: int, rows: int):
+        """The [rows, hidden] bf16 buffer of this rank's partial for ``epoch``."""
+        import torch
+        ptr = lib().gdn_b200_rank_sum_part(ctypes.byref(self.group), epoch)
+        return torch.as_tensor(_DeviceArray(ptr, (rows, self.hidden), "<i2"),
+                               device=self.device).view(torch.bfloat16)
+
+    def acquire(self, epoch: int, stream=None) -> None:
+        _check(lib().gdn_b200_rank_sum_acquire(ctypes.byref(self.group), epoch,
+                                               _ptr(self._err), _stream(stream)))
+
+    def reduce(self, epoch: int, rows: int, shard_out, stream=None, comm_stream=None) -> None:
+        _check(lib().gdn_b200_rank_sum(ctypes.byref(self.group), epoch, rows, _ptr(shard_out),
+                                       _ptr(self._err), _stream(stream), _stream(comm_stream)))
+
+    def status(self, stream=None) -> None:
+        """Synchronises and raises if a wait of the exchange ran out."""
+        _check(lib().gdn_b200_workspace_status(_ptr(self._err), _stream(stream)))
+
+    def close(self) -> None:
+        for p in self._opened:
+            lib().gdn_b200_exchange_close(ctypes.c_void_p(p))
+        self._opened = []
+        if self._own is not None:
             lib().gdn_b200_exchange_free(ctypes.c_void_p(self._own))
             self._own = None
 

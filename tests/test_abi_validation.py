@@ -321,3 +321,26 @@ def test_layer_forward_x_rejects_and_sizes():
     assert G.layer_forward_x_workspace_bytes(cu, 16, 32, 2048) > \
         G.layer_forward_workspace_bytes(cu, 16, 32, 2048) + \
         G.input_side_workspace_bytes(cu, 16, 32, 2048) - 256
+
+
+def test_rank_sum_layout_and_rejections():
+    # two partial buffers + 2 x world staging slots + 256 bytes of flags
+    part = 8192 * 2048 * 2
+    slot = 8192 // 8 * 2048 * 2
+    assert G.lib().gdn_b200_rank_sum_bytes(8192, 2048, 8) == 2 * part + 2 * 8 * slot + 256
+    assert G.lib().gdn_b200_rank_sum_bytes(8190, 2048, 8) == 0      # rows % world
+    assert G.lib().gdn_b200_rank_sum_bytes(64, 2048, 9) == 0        # at most 8 ranks
+    assert G.lib().gdn_b200_rank_sum_bytes(64, 100, 2) == 0         # hidden % 8
+    grp = G.TailGroupV1(0, 2, 64, 2048, 0, (ctypes.c_void_p * G.MAX_RANKS)())
+    st = G.lib().gdn_b200_rank_sum(ctypes.byref(grp), 1, 64, ctypes.c_void_p(256),
+                                   ctypes.c_void_p(256), None, None)
+    assert st == G.INVALID_ARGUMENT and "group" in G.last_error()
+    assert G.lib().gdn_b200_rank_sum_part(ctypes.byref(grp), 1) is None
+    regions = (ctypes.c_void_p * G.MAX_RANKS)(4096, 8192)
+    grp = G.TailGroupV1(0, 2, 64, 2048, 0, regions)
+    assert G.lib().gdn_b200_rank_sum(ctypes.byref(grp), 0, 64, ctypes.c_void_p(256),
+                                     ctypes.c_void_p(256), None, None) == G.INVALID_ARGUMENT
+    assert G.lib().gdn_b200_rank_sum(ctypes.byref(grp), 1, 63, ctypes.c_void_p(256),
+                                     ctypes.c_void_p(256), None, None) == G.INVALID_ARGUMENT
+    assert "multiple of world_size" in G.last_error()
+    assert G.lib().gdn_b200_rank_sum_part(ctypes.byref(grp), 3) == 4096 + 64 * 2048 * 2
