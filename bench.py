@@ -363,6 +363,128 @@ def small_shape_components(dev, stream, iters):
     return comps
 
 
+CFG4_SEQS, CFG4_LEN, CFG4_DECODE = 16, 16384, 256
+
+
+def run_cfg4(args):
+    """The sharded workload: 16 sequences x 16384 tokens of chunked prefill,
+    then one decode step of 256 sequences (f32 state ~ N(0, 0.05)), the heads
+    split over N GPUs (Hv/N and Hk/N per rank, w_out columns sharded), each
+    layer's rank-partial output summed by the copy-engine reduce-scatter
+    (at N > 1) overlapping the next call.  Total work is fixed: "strong"
+    scaling.  One JSON line at rank 0."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import gdn_b200 as G
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    hk, hv = QK_HEADS // world, V_HEADS // world
+    full = G.Geometry(QK_HEADS, V_HEADS, HIDDEN)
+    cu_p = np.arange(CFG4_SEQS + 1, dtype=np.int32) * CFG4_LEN
+    cu_d = np.arange(CFG4_DECODE + 1, dtype=np.int32)
+    Tp, Td = int(cu_p[-1]), CFG4_DECODE
+    shard = (rank, world) if world > 1 else None
+    tp = G.to_device(G.synthetic_layer_inputs(cu_p, full, seed=41, shard=shard), dev)
+    td = G.to_device(G.synthetic_layer_inputs(cu_d, full, seed=42, state_std=0.05, shard=shard), dev)
+    ws_p = torch.empty(G.layer_forward_workspace_bytes(cu_p, hk, hv, HIDDEN), dtype=torch.uint8,
+                       device=dev)
+    ws_d = torch.empty(G.layer_forward_workspace_bytes(cu_d, hk, hv, HIDDEN), dtype=torch.uint8,
+                       device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    comm = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    out_p = torch.empty(Tp, HIDDEN, dtype=torch.bfloat16, device=dev)
+    out_d = torch.empty(Td, HIDDEN, dtype=torch.bfloat16, device=dev)
+    rs = None
+    if world > 1:
+        def exchange(payload):
+            got = [None] * world
+            dist.all_gather_object(got, payload)
+            return got
+        rs = {n: G.RankSum(T, HIDDEN, rank, world, dev, exchange=exchange)
+              for n, T in (("p", Tp), ("d", Td))}
+        shards = {n: [torch.empty(T // world, HIDDEN, dtype=torch.bfloat16, device=dev)
+                      for _ in range(2)] for n, T in (("p", Tp), ("d", Td))}
+    epoch = [0]
+
+    def layer(t, cu, T, out, ws, key, e):
+        if rs is None:
+            G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
+                            t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu, out=out,
+                            workspace=ws, stream=stream)
+            return
+        r = rs[key]
+        r.acquire(e, stream)
+        G.layer_forward(t["q"], t["k"], t["v"], t["a"], t["b"], t["z"], t["A_log"],
+                        t["dt_bias"], t["gamma"], t["w_out"], t["state"], cu,
+                        out=r.part(e, T), workspace=ws, stream=stream)
+        r.reduce(e, T, shards[key][e & 1], stream, comm)
+
+    def step():
+        epoch[0] += 1
+        layer(tp, cu_p, Tp, out_p, ws_p, "p", epoch[0])
+        layer(td, cu_d, Td, out_d, ws_d, "d", epoch[0])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = G.kernel_launches()
+    with ClockSampler(local) as clocks:
+        s.record(stream)
+        for _ in range(args.steps):
+            step()
+        stream.wait_stream(comm)
+        e.record(stream)
+        torch.cuda.synchronize()
+    launches = G.kernel_launches() - launches0
+    ms = s.elapsed_time(e) / args.steps
+    G.workspace_status(ws_p, stream)
+    G.workspace_status(ws_d, stream)
+    if rs is not None:
+        for r in rs.values():
+            r.status(comm)
+        v = torch.tensor([ms], device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        ms = float(v.item())
+    tokens = Tp + Td
+    if rank == 0:
+        line = {
+            "metric": "GDN layer tokens/sec (config 4: 16x16384 prefill then a 256-sequence "
+                      "decode step, head-parallel)",
+            "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded SplitMix64/Box-Muller, benchmark distributions)",
+            "config": {"workload": f"chunked prefill {CFG4_SEQS}x{CFG4_LEN} tokens + tail, then "
+                                   f"a decode step of {CFG4_DECODE} sequences + tail, Hk=16 "
+                                   f"Hv=32 D=128 hidden=2048 over {world} GPU(s)",
+                       "tokens_per_step": tokens,
+                       "parallelism": f"head-parallel tp{world}" + reduce_desc(world, "ce"),
+                       "l2": "inputs larger than L2"},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        for r in rs.values():
+            r.close()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -370,6 +492,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", choices=["cfg1", "cfg4"], default="cfg1",
+                    help="cfg1 (default): the headline 2N x 4096 prefill line; cfg4: 16 x "
+                         "16384 prefill then a 256-sequence decode, head-parallel (strong "
+                         "scaling)")
     ap.add_argument("--component-iters", type=int, default=50,
                     help="calls timed per small-shape component (N=1 only)")
     ap.add_argument("--reduce", choices=["auto", "ce", "fused", "nccl", "rs"], default="auto",
@@ -382,6 +508,9 @@ def main():
         raise SystemExit("--warmup must be at least 3")
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.config == "cfg4":
+        run_cfg4(args)
         return
 
     import numpy as np

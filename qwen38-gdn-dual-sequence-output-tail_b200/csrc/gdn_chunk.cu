@@ -90,10 +90,11 @@ __device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], 
   float acc[kRows];
   if (worker) {
     // Column cc of T in 16-row pieces (keeps the register count low enough
-    // for three CTAs per SM).
-    float a0[kRows], a1[kRows];
+    // for three CTAs per SM).  Two accumulators per row in one f32x2 pair:
+    // one fma.rn.f32x2 does two multiply-adds.
+    float2 a2[kRows];
 #pragma unroll
-    for (int k = 0; k < kRows; ++k) a0[k] = a1[k] = 0.f;
+    for (int k = 0; k < kRows; ++k) a2[k] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int m0 = 0; m0 < kCols; m0 += 16) {
       float tcol[16];
@@ -105,14 +106,14 @@ __device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], 
 #pragma unroll
         for (int m = 0; m < 16; m += 4) {
           const float4 av = *reinterpret_cast<const float4*>(&A[16 * I + rr][m0 + m]);
-          a0[k] += av.x * tcol[m] + av.y * tcol[m + 1];
-          a1[k] += av.z * tcol[m + 2] + av.w * tcol[m + 3];
+          a2[k] = ffma2(make_float2(av.x, av.z), make_float2(tcol[m], tcol[m + 2]), a2[k]);
+          a2[k] = ffma2(make_float2(av.y, av.w), make_float2(tcol[m + 1], tcol[m + 3]), a2[k]);
         }
       }
     }
 #pragma unroll
     for (int k = 0; k < kRows; ++k) {
-      acc[k] = a0[k] + a1[k];
+      acc[k] = a2[k].x + a2[k].y;
       X[r0 + k * kStep][cc] = acc[k];
     }
   }
@@ -124,14 +125,14 @@ __device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], 
 #pragma unroll
     for (int k = 0; k < kRows; ++k) {
       const int rr = r0 + k * kStep;
-      float a0 = 0.f, a1 = 0.f;
+      float2 a2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int m = 0; m < 16; m += 4) {
         const float4 tv = *reinterpret_cast<const float4*>(&T[16 * I + rr][16 * I + m]);
-        a0 += tv.x * xcol[m] + tv.y * xcol[m + 1];
-        a1 += tv.z * xcol[m + 2] + tv.w * xcol[m + 3];
+        a2 = ffma2(make_float2(tv.x, tv.z), make_float2(xcol[m], xcol[m + 2]), a2);
+        a2 = ffma2(make_float2(tv.y, tv.w), make_float2(xcol[m + 1], xcol[m + 3]), a2);
       }
-      acc[k] = -(a0 + a1);
+      acc[k] = -(a2.x + a2.y);
     }
   }
   group_barrier(1 + grp, 128);
