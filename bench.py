@@ -73,10 +73,13 @@ class ClockSampler:
 
     def __init__(self, device_index: int):
         self.device_index = device_index
-        self.samples = []      # (sm_mhz, max_mhz, reason bit mask)
+        self.samples = []      # (monotonic s, sm_mhz, max_mhz, reason bit mask)
         self.proc = None
         self.file = None
         self.thread = None
+        self.nvml = None
+        self.errors = 0
+        self.t0 = 0.0
         self.stop = threading.Event()
 
     def _nvml_handle(self):
@@ -88,25 +91,31 @@ class ClockSampler:
             return pynvml, pynvml.nvmlDeviceGetHandleByIndex(int(ids[self.device_index]))
         return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
 
-    def _poll(self, nv, h):
-        reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-            nv.nvmlDeviceGetCurrentClocksThrottleReasons
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+    def _sample(self, nv, h, reasons, mx):
+        self.samples.append((time.monotonic(), nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                             mx, int(reasons(h))))
+
+    def _poll(self, nv, h, reasons, mx):
         while not self.stop.is_set():
             try:
-                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx,
-                                     int(reasons(h))))
+                self._sample(nv, h, reasons, mx)
             except Exception:
-                pass
+                self.errors += 1
             time.sleep(0.002)
 
     def __enter__(self):
         try:
             nv, h = self._nvml_handle()
-            self.thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
+            reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._sample(nv, h, reasons, mx)        # NVML answers: poll it from a thread
+            self.nvml = (nv, h, reasons, mx)
+            self.thread = threading.Thread(target=self._poll, args=self.nvml, daemon=True)
             self.thread.start()
         except Exception:
             self.thread = None
+            self.nvml = None
             self.file = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
             try:
                 self.proc = subprocess.Popen(
@@ -115,13 +124,25 @@ class ClockSampler:
                     stdout=self.file, stderr=subprocess.DEVNULL)
             except Exception:
                 self.proc = None
-        time.sleep(0.05)
+            time.sleep(0.05)
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
+        t1 = time.monotonic()
         self.stop.set()
         if self.thread is not None:
             self.thread.join(timeout=5)
+            # Samples taken inside the timed region only; if the region was
+            # too short for the poller, one sample right at its end.
+            inside = [x for x in self.samples if self.t0 <= x[0] <= t1]
+            if not inside:
+                try:
+                    self._sample(*self.nvml)
+                    inside = self.samples[-1:]
+                except Exception:
+                    self.errors += 1
+            self.samples = inside
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -136,7 +157,7 @@ class ClockSampler:
                         try:
                             mask = sum(self.REASONS[name] for name, col in self.SMI_COLUMNS.items()
                                        if r[col].strip().lower() == "active")
-                            self.samples.append((float(r[1]), float(r[2]), mask))
+                            self.samples.append((0.0, float(r[1]), float(r[2]), mask))
                         except Exception:
                             continue
                 os.unlink(self.file.name)
@@ -144,13 +165,16 @@ class ClockSampler:
                 pass
 
     def summary(self):
-        sm = [x[0] for x in self.samples]
-        mx = max((x[1] for x in self.samples), default=0.0)
+        sm = [x[1] for x in self.samples]
+        mx = max((x[2] for x in self.samples), default=0.0)
         reasons = sorted(name for name, bit in self.REASONS.items()
-                         if any(x[2] & bit for x in self.samples))
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": reasons, "samples": len(sm),
-                "source": "nvml, 2 ms" if self.thread is not None else "nvidia-smi, 20 ms"}
+                         if any(x[3] & bit for x in self.samples))
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+               "reasons": reasons, "samples": len(sm),
+               "source": "nvml, 2 ms" if self.thread is not None else "nvidia-smi, 20 ms"}
+        if self.errors:
+            out["sample_errors"] = self.errors
+        return out
 
 
 def workload_desc(nseq: int) -> str:
