@@ -73,72 +73,131 @@ __device__ __forceinline__ void group_barrier(int id, int threads) {
 
 // ============================================================ prep =====
 
-// Block row I of T = (I + A)^-1 (16x16 blocks, diagonal blocks already in T):
-// T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ for every J < I at once.  T's
-// strictly upper blocks are zero, so the inner sum runs over m in [0, 16 I)
-// for every column and all trip counts are compile-time constants.
-// Thread u -> column cc = u % (16 I) and rows r0 + k * rstep.
-template <int I>
-__device__ __forceinline__ void merge_block_row(float (*A)[68], float (*T)[68], float (*X)[49],
-                                                int u, int grp, bool live) {
-  constexpr int kCols = 16 * I;
-  constexpr int kStep = 128 / kCols;              // 8, 4, 2
-  constexpr int kRows = (16 + kStep - 1) / kStep; // 2, 4, 8
-  const int cc = u % kCols;
-  const int r0 = u / kCols;
-  const bool worker = live && r0 < kStep;
-  float acc[kRows];
-  if (worker) {
-    // Column cc of T in 16-row pieces (keeps the register count low enough
-    // for three CTAs per SM).  Two accumulators per row in one f32x2 pair:
-    // one fma.rn.f32x2 does two multiply-adds.
-    float2 a2[kRows];
+// T = (I + A)^-1 by block doubling, once the four 16x16 diagonal blocks of T
+// are in place (M holds A below them).  For a unit lower-triangular
+// [[M1, 0], [M21, M2]] the inverse is [[T1, 0], [-T2 M21 T1, T2]], so
+//   level 1: T_10 = -T_11 (A_10 T_00),  T_32 = -T_33 (A_32 T_22)
+//   level 2: X = [A_20 A_21; A_30 A_31] [T_00 0; T_10 T_11]   (32 x 32)
+//            [T_20 T_21; T_30 T_31] = -[T_22 0; T_32 T_33] X
+// in four phases of one group of 128 threads.  The products X go to the
+// strictly upper blocks of M, which the inverse never reads (the T store
+// masks them to zero).  Warp w of the group takes rows w + 4 (lane / 16) and
+// that + 8 of every output block, lane % 16 its column: all 128 threads carry
+// the same number of multiply-adds in every phase, the loop bounds are
+// warp-uniform, and the two rows of an instruction are 4 apart (16 banks).
+// Products run on f32x2 pairs along the summation index (even and odd terms).
+__device__ __forceinline__ float2 col_pair(float (*M)[68], int m, int c) {
+  return make_float2(M[m][c], M[m + 1][c]);
+}
+__device__ __forceinline__ float2 row_pair(float (*M)[68], int r, int m) {
+  return *reinterpret_cast<const float2*>(&M[r][m]);
+}
+__device__ __forceinline__ float pair_sum(float2 v) { return v.x + v.y; }
+
+__device__ __forceinline__ void invert_by_doubling(float (*M)[68], int u, int grp, bool live) {
+  const int c = u & 15;
+  const int r0 = (u >> 5) + 4 * ((u >> 4) & 1);
+  // Level 1, products: X_10 -> block (0, 1), X_32 -> block (2, 3).
+  if (live) {
+    float2 acc[2][2] = {};
 #pragma unroll
-    for (int k = 0; k < kRows; ++k) a2[k] = make_float2(0.f, 0.f);
+    for (int m = 0; m < 16; m += 2) {
+      const float2 t00 = col_pair(M, m, c), t22 = col_pair(M, 32 + m, 32 + c);
 #pragma unroll
-    for (int m0 = 0; m0 < kCols; m0 += 16) {
-      float tcol[16];
-#pragma unroll
-      for (int m = 0; m < 16; ++m) tcol[m] = T[m0 + m][cc];
-#pragma unroll
-      for (int k = 0; k < kRows; ++k) {
-        const int rr = r0 + k * kStep;
-#pragma unroll
-        for (int m = 0; m < 16; m += 4) {
-          const float4 av = *reinterpret_cast<const float4*>(&A[16 * I + rr][m0 + m]);
-          a2[k] = ffma2(make_float2(av.x, av.z), make_float2(tcol[m], tcol[m + 2]), a2[k]);
-          a2[k] = ffma2(make_float2(av.y, av.w), make_float2(tcol[m + 1], tcol[m + 3]), a2[k]);
-        }
+      for (int k = 0; k < 2; ++k) {
+        const int r = r0 + 8 * k;
+        acc[k][0] = ffma2(row_pair(M, 16 + r, m), t00, acc[k][0]);
+        acc[k][1] = ffma2(row_pair(M, 48 + r, 32 + m), t22, acc[k][1]);
       }
     }
 #pragma unroll
-    for (int k = 0; k < kRows; ++k) {
-      acc[k] = a2[k].x + a2[k].y;
-      X[r0 + k * kStep][cc] = acc[k];
+    for (int k = 0; k < 2; ++k) {
+      M[r0 + 8 * k][16 + c] = pair_sum(acc[k][0]);
+      M[32 + r0 + 8 * k][48 + c] = pair_sum(acc[k][1]);
     }
   }
   group_barrier(1 + grp, 128);
-  if (worker) {
-    float xcol[16];
+  // Level 1, T_10 = -T_11 X_10 and T_32 = -T_33 X_32 (over A_10, A_32).
+  if (live) {
+    float2 acc[2][2] = {};
 #pragma unroll
-    for (int m = 0; m < 16; ++m) xcol[m] = X[m][cc];
+    for (int m = 0; m < 16; m += 2) {
+      const float2 x10 = col_pair(M, m, 16 + c), x32 = col_pair(M, 32 + m, 48 + c);
 #pragma unroll
-    for (int k = 0; k < kRows; ++k) {
-      const int rr = r0 + k * kStep;
-      float2 a2 = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int m = 0; m < 16; m += 4) {
-        const float4 tv = *reinterpret_cast<const float4*>(&T[16 * I + rr][16 * I + m]);
-        a2 = ffma2(make_float2(tv.x, tv.z), make_float2(xcol[m], xcol[m + 2]), a2);
-        a2 = ffma2(make_float2(tv.y, tv.w), make_float2(xcol[m + 1], xcol[m + 3]), a2);
+      for (int k = 0; k < 2; ++k) {
+        const int r = r0 + 8 * k;
+        acc[k][0] = ffma2(row_pair(M, 16 + r, 16 + m), x10, acc[k][0]);
+        acc[k][1] = ffma2(row_pair(M, 48 + r, 48 + m), x32, acc[k][1]);
       }
-      acc[k] = -(a2.x + a2.y);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      M[16 + r0 + 8 * k][c] = -pair_sum(acc[k][0]);
+      M[48 + r0 + 8 * k][32 + c] = -pair_sum(acc[k][1]);
     }
   }
   group_barrier(1 + grp, 128);
-  if (worker) {
+  // Level 2, products: X_20 -> (0, 2), X_21 -> (0, 3), X_30 -> (1, 2),
+  // X_31 -> (1, 3).
+  if (live) {
+    float2 acc[2][4] = {};
 #pragma unroll
-    for (int k = 0; k < kRows; ++k) T[16 * I + r0 + k * kStep][cc] = acc[k];
+    for (int m = 0; m < 32; m += 2) {
+      const float2 tlo = col_pair(M, m, c);          // [T_00; T_10], column c
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int r = r0 + 8 * k;
+        acc[k][0] = ffma2(row_pair(M, 32 + r, m), tlo, acc[k][0]);
+        acc[k][2] = ffma2(row_pair(M, 48 + r, m), tlo, acc[k][2]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 16; m += 2) {
+      const float2 t11 = col_pair(M, 16 + m, 16 + c);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int r = r0 + 8 * k;
+        acc[k][1] = ffma2(row_pair(M, 32 + r, 16 + m), t11, acc[k][1]);
+        acc[k][3] = ffma2(row_pair(M, 48 + r, 16 + m), t11, acc[k][3]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int r = r0 + 8 * k;
+      M[r][32 + c] = pair_sum(acc[k][0]);
+      M[r][48 + c] = pair_sum(acc[k][1]);
+      M[16 + r][32 + c] = pair_sum(acc[k][2]);
+      M[16 + r][48 + c] = pair_sum(acc[k][3]);
+    }
+  }
+  group_barrier(1 + grp, 128);
+  // Level 2, the lower-left 32 x 32 block of T (over A_20 .. A_31).
+  if (live) {
+    float2 acc[2][4] = {};
+#pragma unroll
+    for (int m = 0; m < 16; m += 2) {
+      const float2 x20 = col_pair(M, m, 32 + c), x21 = col_pair(M, m, 48 + c);
+      const float2 x30 = col_pair(M, 16 + m, 32 + c), x31 = col_pair(M, 16 + m, 48 + c);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int r = r0 + 8 * k;
+        const float2 t22 = row_pair(M, 32 + r, 32 + m);
+        const float2 t32 = row_pair(M, 48 + r, 32 + m);
+        const float2 t33 = row_pair(M, 48 + r, 48 + m);
+        acc[k][0] = ffma2(t22, x20, acc[k][0]);
+        acc[k][1] = ffma2(t22, x21, acc[k][1]);
+        acc[k][2] = ffma2(t33, x30, ffma2(t32, x20, acc[k][2]));
+        acc[k][3] = ffma2(t33, x31, ffma2(t32, x21, acc[k][3]));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int r = r0 + 8 * k;
+      M[32 + r][c] = -pair_sum(acc[k][0]);
+      M[32 + r][16 + c] = -pair_sum(acc[k][1]);
+      M[48 + r][c] = -pair_sum(acc[k][2]);
+      M[48 + r][16 + c] = -pair_sum(acc[k][3]);
+    }
   }
   group_barrier(1 + grp, 128);
 }
@@ -149,8 +208,8 @@ constexpr int kPrepThreads = 256;
 struct PrepSmem {
   uint8_t kq[kKQBytes];     // [K;Q] tile (1024-aligned): raw q/k land here by TMA
                             // and are normalised in place
-  float amat[2][64][68];    // A, overwritten in place by T = (I + A)^-1
-  float xs[2][16][49];      // block-merge temporaries (odd stride: no bank conflicts)
+  float amat[2][64][68];    // A, overwritten in place by T = (I + A)^-1; the
+                            // strictly upper blocks hold the inverse's products
   float g[2][64];           // cumsum G
   float e1[2][64];          // exp(g_t) = exp(G_t - G_{t-1})
   float beta[2][64];
@@ -308,7 +367,6 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
     // I of T is formed, and T's strictly upper part equals A's (zero).
     float (*A)[68] = sm.amat[grp];
     float (*T)[68] = sm.amat[grp];
-    float (*X)[49] = sm.xs[grp];
 
     for (int hp = 0; hp < group; hp += 2) {
       const int hl = hp + grp;
@@ -437,32 +495,38 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
         if (next < units) load_unit(next);
       }
 
-      // T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution
-      // (one thread per block column), then block rows I = 1..3:
-      //   T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ.
+      // T = (I + A)^-1: the 16x16 diagonal blocks by forward substitution
+      // (one thread per block column; x[rr] = 0 above the diagonal), then
+      // block doubling (invert_by_doubling).  The substitution sums run on
+      // f32x2 pairs (even and odd terms), halving the dependent chain.
       const bool diag = active && ok && u < 64;
       const int bl = u >> 4, dc = u & 15, o = bl * 16;
-      float x[16];
+      float2 x2[8];
       if (diag) {
   #pragma unroll
         for (int rr = 0; rr < 16; ++rr) {
-          float acc = (rr == dc) ? 1.f : 0.f;
+          float2 sacc = make_float2(0.f, 0.f);
   #pragma unroll
-          for (int m = 0; m < rr; ++m) acc -= A[o + rr][o + m] * x[m];
-          x[rr] = acc;
+          for (int m = 0; m + 1 < rr; m += 2)
+            sacc = ffma2(*reinterpret_cast<const float2*>(&A[o + rr][o + m]), x2[m >> 1], sacc);
+          float v = ((rr == dc) ? 1.f : 0.f) - (sacc.x + sacc.y);
+          if (rr & 1) v -= A[o + rr][o + rr - 1] * x2[(rr - 1) >> 1].x;
+          if (rr & 1) x2[rr >> 1].y = v; else x2[rr >> 1].x = v;
         }
       }
       group_barrier(1 + grp, 128);  // every read of the diagonal A blocks is done
       if (diag) {
   #pragma unroll
-        for (int rr = 0; rr < 16; ++rr) T[o + rr][o + dc] = x[rr];
+        for (int rr = 0; rr < 16; rr += 2) {
+          T[o + rr][o + dc] = x2[rr >> 1].x;
+          T[o + rr + 1][o + dc] = x2[rr >> 1].y;
+        }
       }
       group_barrier(1 + grp, 128);
-      merge_block_row<1>(A, T, X, u, grp, active && ok);
-      merge_block_row<2>(A, T, X, u, grp, active && ok);
-      merge_block_row<3>(A, T, X, u, grp, active && ok);
+      invert_by_doubling(T, u, grp, active && ok);
       // Store T as K-rows j of the MN-major operand image (hi/lo pair):
-      // thread -> column j = u / 2, rows [32 (u % 2), +32).
+      // thread -> column j = u / 2, rows [32 (u % 2), +32); entries above the
+      // diagonal are zero (the upper blocks of M hold scratch).
       if (active && ok) {
         const int j = u >> 1;
         const int i0 = (u & 1) * 32;
@@ -470,8 +534,10 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
         for (int c = 0; c < 4; ++c) {
           uint32_t hi[4], lo[4];
   #pragma unroll
-          for (int p = 0; p < 4; ++p)
-            split_bf16x2(T[i0 + 8 * c + 2 * p][j], T[i0 + 8 * c + 2 * p + 1][j], hi[p], lo[p]);
+          for (int p = 0; p < 4; ++p) {
+            const int i = i0 + 8 * c + 2 * p;
+            split_bf16x2(i >= j ? T[i][j] : 0.f, i + 1 >= j ? T[i + 1][j] : 0.f, hi[p], lo[p]);
+          }
           const uint32_t off = sw128_chunk(j, (i0 >> 3) + c);
           *reinterpret_cast<uint4*>(rec + kRecTHi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
           *reinterpret_cast<uint4*>(rec + kRecTLo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
