@@ -89,10 +89,20 @@ __device__ __forceinline__ void group_barrier(int id, int threads) {
 __device__ __forceinline__ float2 col_pair(float (*M)[68], int m, int c) {
   return make_float2(M[m][c], M[m + 1][c]);
 }
-__device__ __forceinline__ float2 row_pair(float (*M)[68], int r, int m) {
-  return *reinterpret_cast<const float2*>(&M[r][m]);
+// M[r][m .. m+3] as two pairs (one 16-byte load; m % 4 == 0).
+__device__ __forceinline__ void row_quad(float (*M)[68], int r, int m, float2& lo, float2& hi) {
+  const float4 q = *reinterpret_cast<const float4*>(&M[r][m]);
+  lo = make_float2(q.x, q.y);
+  hi = make_float2(q.z, q.w);
 }
 __device__ __forceinline__ float pair_sum(float2 v) { return v.x + v.y; }
+// acc += M[r][m .. m+3] . (b0, b1), b0 = column values at m, m+1 and b1 at m+2, m+3.
+__device__ __forceinline__ float2 quad_fma(float (*M)[68], int r, int m, float2 b0, float2 b1,
+                                           float2 acc) {
+  float2 lo, hi;
+  row_quad(M, r, m, lo, hi);
+  return ffma2(hi, b1, ffma2(lo, b0, acc));
+}
 
 __device__ __forceinline__ void invert_by_doubling(float (*M)[68], int u, int grp, bool live) {
   const int c = u & 15;
@@ -101,13 +111,14 @@ __device__ __forceinline__ void invert_by_doubling(float (*M)[68], int u, int gr
   if (live) {
     float2 acc[2][2] = {};
 #pragma unroll
-    for (int m = 0; m < 16; m += 2) {
-      const float2 t00 = col_pair(M, m, c), t22 = col_pair(M, 32 + m, 32 + c);
+    for (int m = 0; m < 16; m += 4) {
+      const float2 t00a = col_pair(M, m, c), t00b = col_pair(M, m + 2, c);
+      const float2 t22a = col_pair(M, 32 + m, 32 + c), t22b = col_pair(M, 34 + m, 32 + c);
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int r = r0 + 8 * k;
-        acc[k][0] = ffma2(row_pair(M, 16 + r, m), t00, acc[k][0]);
-        acc[k][1] = ffma2(row_pair(M, 48 + r, 32 + m), t22, acc[k][1]);
+        acc[k][0] = quad_fma(M, 16 + r, m, t00a, t00b, acc[k][0]);
+        acc[k][1] = quad_fma(M, 48 + r, 32 + m, t22a, t22b, acc[k][1]);
       }
     }
 #pragma unroll
@@ -121,13 +132,14 @@ __device__ __forceinline__ void invert_by_doubling(float (*M)[68], int u, int gr
   if (live) {
     float2 acc[2][2] = {};
 #pragma unroll
-    for (int m = 0; m < 16; m += 2) {
-      const float2 x10 = col_pair(M, m, 16 + c), x32 = col_pair(M, 32 + m, 48 + c);
+    for (int m = 0; m < 16; m += 4) {
+      const float2 x10a = col_pair(M, m, 16 + c), x10b = col_pair(M, m + 2, 16 + c);
+      const float2 x32a = col_pair(M, 32 + m, 48 + c), x32b = col_pair(M, 34 + m, 48 + c);
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int r = r0 + 8 * k;
-        acc[k][0] = ffma2(row_pair(M, 16 + r, 16 + m), x10, acc[k][0]);
-        acc[k][1] = ffma2(row_pair(M, 48 + r, 48 + m), x32, acc[k][1]);
+        acc[k][0] = quad_fma(M, 16 + r, 16 + m, x10a, x10b, acc[k][0]);
+        acc[k][1] = quad_fma(M, 48 + r, 48 + m, x32a, x32b, acc[k][1]);
       }
     }
 #pragma unroll
@@ -142,23 +154,23 @@ __device__ __forceinline__ void invert_by_doubling(float (*M)[68], int u, int gr
   if (live) {
     float2 acc[2][4] = {};
 #pragma unroll
-    for (int m = 0; m < 32; m += 2) {
-      const float2 tlo = col_pair(M, m, c);          // [T_00; T_10], column c
+    for (int m = 0; m < 32; m += 4) {
+      const float2 ta = col_pair(M, m, c), tb = col_pair(M, m + 2, c);   // [T_00; T_10]
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int r = r0 + 8 * k;
-        acc[k][0] = ffma2(row_pair(M, 32 + r, m), tlo, acc[k][0]);
-        acc[k][2] = ffma2(row_pair(M, 48 + r, m), tlo, acc[k][2]);
+        acc[k][0] = quad_fma(M, 32 + r, m, ta, tb, acc[k][0]);
+        acc[k][2] = quad_fma(M, 48 + r, m, ta, tb, acc[k][2]);
       }
     }
 #pragma unroll
-    for (int m = 0; m < 16; m += 2) {
-      const float2 t11 = col_pair(M, 16 + m, 16 + c);
+    for (int m = 0; m < 16; m += 4) {
+      const float2 ta = col_pair(M, 16 + m, 16 + c), tb = col_pair(M, 18 + m, 16 + c);   // T_11
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int r = r0 + 8 * k;
-        acc[k][1] = ffma2(row_pair(M, 32 + r, 16 + m), t11, acc[k][1]);
-        acc[k][3] = ffma2(row_pair(M, 48 + r, 16 + m), t11, acc[k][3]);
+        acc[k][1] = quad_fma(M, 32 + r, 16 + m, ta, tb, acc[k][1]);
+        acc[k][3] = quad_fma(M, 48 + r, 16 + m, ta, tb, acc[k][3]);
       }
     }
 #pragma unroll
@@ -175,19 +187,22 @@ __device__ __forceinline__ void invert_by_doubling(float (*M)[68], int u, int gr
   if (live) {
     float2 acc[2][4] = {};
 #pragma unroll
-    for (int m = 0; m < 16; m += 2) {
-      const float2 x20 = col_pair(M, m, 32 + c), x21 = col_pair(M, m, 48 + c);
-      const float2 x30 = col_pair(M, 16 + m, 32 + c), x31 = col_pair(M, 16 + m, 48 + c);
+    for (int m = 0; m < 16; m += 4) {
+      const float2 x20a = col_pair(M, m, 32 + c), x20b = col_pair(M, m + 2, 32 + c);
+      const float2 x21a = col_pair(M, m, 48 + c), x21b = col_pair(M, m + 2, 48 + c);
+      const float2 x30a = col_pair(M, 16 + m, 32 + c), x30b = col_pair(M, 18 + m, 32 + c);
+      const float2 x31a = col_pair(M, 16 + m, 48 + c), x31b = col_pair(M, 18 + m, 48 + c);
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int r = r0 + 8 * k;
-        const float2 t22 = row_pair(M, 32 + r, 32 + m);
-        const float2 t32 = row_pair(M, 48 + r, 32 + m);
-        const float2 t33 = row_pair(M, 48 + r, 48 + m);
-        acc[k][0] = ffma2(t22, x20, acc[k][0]);
-        acc[k][1] = ffma2(t22, x21, acc[k][1]);
-        acc[k][2] = ffma2(t33, x30, ffma2(t32, x20, acc[k][2]));
-        acc[k][3] = ffma2(t33, x31, ffma2(t32, x21, acc[k][3]));
+        float2 t22a, t22b, t32a, t32b, t33a, t33b;
+        row_quad(M, 32 + r, 32 + m, t22a, t22b);
+        row_quad(M, 48 + r, 32 + m, t32a, t32b);
+        row_quad(M, 48 + r, 48 + m, t33a, t33b);
+        acc[k][0] = ffma2(t22b, x20b, ffma2(t22a, x20a, acc[k][0]));
+        acc[k][1] = ffma2(t22b, x21b, ffma2(t22a, x21a, acc[k][1]));
+        acc[k][2] = ffma2(t33b, x30b, ffma2(t33a, x30a, ffma2(t32b, x20b, ffma2(t32a, x20a, acc[k][2]))));
+        acc[k][3] = ffma2(t33b, x31b, ffma2(t33a, x31a, ffma2(t32b, x21b, ffma2(t32a, x21a, acc[k][3]))));
       }
     }
 #pragma unroll
@@ -311,7 +326,8 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
       // tile is read twice from shared memory instead of being held in
       // registers.
       const bool live_row = landed && tok < n;
-      float ss = 0.f;
+      // Sum of squares on f32x2 pairs (the two halves of each bf16x2 word).
+      float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 v = live_row
@@ -320,24 +336,28 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const float x0 = bf16lo_f32(w[p]), x1 = bf16hi_f32(w[p]);
-          ss += x0 * x0 + x1 * x1;
+          const float2 x = bf16x2_f32x2(w[p]);
+          ss2 = ffma2(x, x, ss2);
         }
       }
+      float ss = ss2.x + ss2.y;
       ss += __shfl_xor_sync(0xffffffffu, ss, 1);
       const float rs = rsqrtf(ss * (1.0f / 128.0f) + 1.0e-6f / 128.0f) * l2gamma;
+      const float2 rs2 = make_float2(rs, rs);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 v = live_row
                             ? *reinterpret_cast<const uint4*>(tile + half * 16384u + sw128_chunk(r, c))
                             : make_uint4(0u, 0u, 0u, 0u);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        uint4 o;
-        o.x = pack_bf16x2(bf16lo_f32(w[0]) * rs, bf16hi_f32(w[0]) * rs);
-        o.y = pack_bf16x2(bf16lo_f32(w[1]) * rs, bf16hi_f32(w[1]) * rs);
-        o.z = pack_bf16x2(bf16lo_f32(w[2]) * rs, bf16hi_f32(w[2]) * rs);
-        o.w = pack_bf16x2(bf16lo_f32(w[3]) * rs, bf16hi_f32(w[3]) * rs);
-        *reinterpret_cast<uint4*>(tile + half * 16384u + sw128_chunk(r, c)) = o;
+        uint32_t ow[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float2 y = fmul2(bf16x2_f32x2(w[p]), rs2);
+          ow[p] = pack_bf16x2(y.x, y.y);
+        }
+        *reinterpret_cast<uint4*>(tile + half * 16384u + sw128_chunk(r, c)) =
+            make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
     }
     fence_proxy_async_smem();
@@ -427,31 +447,36 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
         // TMEM row of this lane, 16 columns at a time.
         const uint32_t base = tmem_addr(tmem, quarter * 32, 0);
         if (u < 64) {
-          // Lane u holds row u of K K^T = column u (symmetric).  Column u of A:
-          // A[i][u] = beta_i KK_iu exp(G_i - G_u) for u < i < n, with the decay
-          // formed as a running product of the per-token exp(g).  The factors
-          // are read into registers first so the loop carries no shared-memory
-          // loads behind the stores to A.
+          // Lane u holds row u of K K^T: A[u][j] = beta_u KK_uj exp(G_u - G_j)
+          // for j < u (beta_u = 0 past the chunk), the decay a running
+          // product of the per-token exp(g) towards smaller j; each
+          // 16-column piece goes to row u of A as four 16-byte stores.
+          const float bu = sm.beta[grp][u];
           float d = 1.f;
+          float e1_up = 1.f;                 // exp(g) of the token after the piece
   #pragma unroll
-          for (int c = 0; c < 64; c += 16) {
+          for (int c = 48; c >= 0; c -= 16) {
             uint32_t r[16];
             tmem_ld16(base + c, r);
-            float e1v[16], bv[16];
+            float e1v[16];
   #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
               const float4 ev = *reinterpret_cast<const float4*>(&sm.e1[grp][c + 4 * q4]);
-              const float4 bb = *reinterpret_cast<const float4*>(&sm.beta[grp][c + 4 * q4]);
               e1v[4 * q4] = ev.x; e1v[4 * q4 + 1] = ev.y; e1v[4 * q4 + 2] = ev.z; e1v[4 * q4 + 3] = ev.w;
-              bv[4 * q4] = bb.x; bv[4 * q4 + 1] = bb.y; bv[4 * q4 + 2] = bb.z; bv[4 * q4 + 3] = bb.w;
             }
             tmem_ld_wait();
+            float av[16];
   #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int i = c + j;
-              d = (i > u) ? d * e1v[j] : 1.f;
-              A[i][u] = (i > u && i < n) ? bv[j] * __uint_as_float(r[j]) * d : 0.f;
+            for (int jj = 15; jj >= 0; --jj) {
+              const int j = c + jj;
+              d = (j < u) ? d * (jj == 15 ? e1_up : e1v[jj + 1]) : 1.f;
+              av[jj] = (j < u) ? bu * __uint_as_float(r[jj]) * d : 0.f;
             }
+            e1_up = e1v[0];
+  #pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+              *reinterpret_cast<float4*>(&A[u][c + 4 * q4]) =
+                  make_float4(av[4 * q4], av[4 * q4 + 1], av[4 * q4 + 2], av[4 * q4 + 3]);
           }
         } else {
           // Lane 64+i holds row i of Q K^T: P[i][j] = QK_ij exp(G_i - G_j),

@@ -189,6 +189,17 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   return f2_unpack(d);
 }
 
+// a * b per lane, rounded (mul.rn).
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+  return f2_unpack(d);
+}
+// The two bf16 halves of a packed word as an f32 pair (low element first).
+__device__ __forceinline__ float2 bf16x2_f32x2(uint32_t w) {
+  return make_float2(bf16lo_f32(w), bf16hi_f32(w));
+}
+
 // ---------------------------------------------------------- mbarrier -----
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
