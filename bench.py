@@ -45,7 +45,7 @@ CHUNK_MFLOP = 11.62    # prefill core work per (chunk of 64, v-head)
 # DRAM bytes (read + write) per call of the chunk core on the single-GPU
 # workload, from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum
 # of the prep and state kernels on this workload).
-CHUNK_CORE_DRAM_BYTES = {"prep": 68933888 + 121297152, "state": 244374272 + 46572032}
+CHUNK_CORE_DRAM_BYTES = {"prep": 68519680 + 116966656, "state": 244397056 + 46440960}
 
 
 def load_peaks():
