@@ -71,12 +71,40 @@ tail_prologue_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict_
 
 // ---------------------------------------------------------------- GEMM --
 
+// Unit -> output tile.  Units below full_units are whole BM x BN tiles (unit
+// = tile * splits + split); when the last wave of tiles would leave SMs idle,
+// each remaining tile runs as two BM x BN/2 halves (units full_units + 2 r
+// and + 1), so that wave takes about half as long.
+struct TileRef {
+  int tm, tn, split, col0, width;
+};
+template <int BN>
+__device__ __forceinline__ TileRef tile_of(int unit, int tiles_n, int splits, int full_units) {
+  TileRef t;
+  int tile, half = -1;
+  if (unit < full_units) {
+    t.split = unit % splits;
+    tile = unit / splits;
+  } else {
+    t.split = 0;
+    tile = full_units / splits + ((unit - full_units) >> 1);
+    half = (unit - full_units) & 1;
+  }
+  t.tn = tile % tiles_n;
+  t.tm = tile / tiles_n;
+  t.col0 = t.tn * BN + (half > 0 ? BN / 2 : 0);
+  t.width = half >= 0 ? BN / 2 : BN;
+  return t;
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 tail_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                 const __grid_constant__ CUtensorMap tmap_b, uint16_t* __restrict__ out,
+                 const __grid_constant__ CUtensorMap tmap_b,
+                 const __grid_constant__ CUtensorMap tmap_b_half, uint16_t* __restrict__ out,
                  float* __restrict__ out_f32, int M, int N, int tiles_m, int tiles_n, int splits,
-                 int kblocks_total, int kblocks_per_split, uint32_t* err) {
+                 int kblocks_total, int kblocks_per_split, int full_units, int total_units,
+                 uint32_t* err) {
   using L = GemmSmem<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -89,7 +117,6 @@ tail_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int total_units = tiles_m * tiles_n * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGemmStages; ++s) {
@@ -103,6 +130,7 @@ tail_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     fence_barrier_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (full_units < total_units) tma_prefetch_desc(&tmap_b_half);
   }
   if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
   tmem_fence_before();
@@ -116,33 +144,35 @@ tail_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t phase = 0;
       bool ok = true;
       for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
-        const int split = unit % splits;
-        const int tile = unit / splits;
-        const int tn = tile % tiles_n;
-        const int tm = tile / tiles_n;
-        const int kb0 = split * kblocks_per_split;
+        const TileRef t = tile_of<BN>(unit, tiles_n, splits, full_units);
+        const bool whole = t.width == BN;
+        const int kb0 = t.split * kblocks_per_split;
         const int kb1 = min(kb0 + kblocks_per_split, kblocks_total);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, err)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          mbar_arrive_expect_tx(&full[stage], whole ? L::kStageBytes
+                                                    : L::kABytes + L::kBBytes / 2);
           uint8_t* sa = smem + stage * L::kStageBytes;
-          tma_load_2d(sa, &tmap_a, &full[stage], kb * kGemmBK, tm * kGemmBM);
-          tma_load_2d(sa + L::kABytes, &tmap_b, &full[stage], kb * kGemmBK, tn * BN);
+          tma_load_2d(sa, &tmap_a, &full[stage], kb * kGemmBK, t.tm * kGemmBM);
+          tma_load_2d(sa + L::kABytes, whole ? &tmap_b : &tmap_b_half, &full[stage],
+                      kb * kGemmBK, t.col0);
           if (++stage == kGemmStages) { stage = 0; phase ^= 1u; }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kGemmBM, BN, false, false);
+      constexpr uint32_t idesc_whole = umma_idesc_bf16(kGemmBM, BN, false, false);
+      constexpr uint32_t idesc_half = umma_idesc_bf16(kGemmBM, BN / 2, false, false);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int unit = blockIdx.x; unit < total_units && ok; unit += gridDim.x) {
-        const int split = unit % splits;
-        const int kb0 = split * kblocks_per_split;
+        const TileRef t = tile_of<BN>(unit, tiles_n, splits, full_units);
+        const uint32_t idesc = t.width == BN ? idesc_whole : idesc_half;
+        const int kb0 = t.split * kblocks_per_split;
         const int kb1 = min(kb0 + kblocks_per_split, kblocks_total);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err)) break;
         tmem_fence_after();
@@ -171,20 +201,18 @@ tail_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x) {
-      const int tile = unit / splits;
-      const int tn = tile % tiles_n;
-      const int tm = tile / tiles_n;
+      const TileRef t = tile_of<BN>(unit, tiles_n, splits, full_units);
       if (!mbar_wait(&tfull[acc], acc_phase, err)) break;
       tmem_fence_after();
-      const int row = tm * kGemmBM + quarter * 32 + lane;
+      const int row = t.tm * kGemmBM + quarter * 32 + lane;
       const uint32_t tbase = tmem_addr(tmem_base, quarter * 32, acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+      for (int c = 0; c < t.width; c += 16) {
         uint32_t r[16];
         tmem_ld16(tbase + c, r);
         tmem_ld_wait();
         if (row < M) {
-          const int64_t off = static_cast<int64_t>(row) * N + tn * BN + c;
+          const int64_t off = static_cast<int64_t>(row) * N + t.col0 + c;
           if (splits == 1) {
             uint4 w0, w1;
             w0.x = pack_bf16x2(__uint_as_float(r[0]), __uint_as_float(r[1]));
@@ -200,8 +228,7 @@ tail_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
           } else {
             // Split-K partial: slice `split` of the [splits, M, N] f32 scratch,
             // summed in a fixed order afterwards (deterministic).
-            const int split = unit % splits;
-            float4* dst = reinterpret_cast<float4*>(out_f32 + static_cast<int64_t>(split) * M * N + off);
+            float4* dst = reinterpret_cast<float4*>(out_f32 + static_cast<int64_t>(t.split) * M * N + off);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
@@ -507,6 +534,7 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t co
 
 struct TailGemmPlan {
   int bn, tiles_m, tiles_n, splits, kblocks_total, kblocks_per_split, grid;
+  int full_units, total_units;   // persistent kernel: whole tiles, all units
   bool cluster;   // split-K reduced inside a thread-block cluster (M <= 128)
 };
 
@@ -560,6 +588,15 @@ TailGemmPlan plan_tail_gemm(int64_t M, int N, int K) {
   p.splits = (p.kblocks_total + p.kblocks_per_split - 1) / p.kblocks_per_split;
   const int units = tiles * p.splits;
   p.grid = units < sms ? units : sms;
+  p.full_units = units;
+  p.total_units = units;
+  // A last wave of whole tiles that would fill at most half of the CTAs
+  // runs as twice as many half-width tiles instead.
+  const int rem = units % p.grid;
+  if (p.splits == 1 && p.bn == 256 && units > p.grid && rem > 0 && 2 * rem <= p.grid) {
+    p.full_units = units - rem;
+    p.total_units = p.full_units + 2 * rem;
+  }
   return p;
 }
 
@@ -588,16 +625,17 @@ cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uin
 }
 
 template <int BN>
-static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, uint16_t* out,
-                                  float* ws, int64_t M, int N, const TailGemmPlan& p,
-                                  uint32_t* err, cudaStream_t stream) {
+static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb,
+                                  const CUtensorMap& tb_half, uint16_t* out, float* ws, int64_t M,
+                                  int N, const TailGemmPlan& p, uint32_t* err,
+                                  cudaStream_t stream) {
   const uint32_t smem = GemmSmem<BN>::kTotal;
   cudaError_t e = cudaFuncSetAttribute(tail_gemm_kernel<BN>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   tail_gemm_kernel<BN><<<p.grid, kGemmThreads, smem, stream>>>(
-      ta, tb, out, ws, static_cast<int>(M), N, p.tiles_m, p.tiles_n, p.splits, p.kblocks_total,
-      p.kblocks_per_split, err);
+      ta, tb, tb_half, out, ws, static_cast<int>(M), N, p.tiles_m, p.tiles_n, p.splits,
+      p.kblocks_total, p.kblocks_per_split, p.full_units, p.total_units, err);
   e = cudaGetLastError();
   if (e == cudaSuccess) note_launches();
   return e;
@@ -638,9 +676,14 @@ cudaError_t launch_tail_gemm(const uint16_t* a, const uint16_t* w, uint16_t* out
     if (ec == cudaSuccess) note_launches();
     return ec;
   }
-  cudaError_t e = (p.bn == 256)   ? launch_gemm_bn<256>(ta, tb, out, ws, M, N, p, err, stream)
-                  : (p.bn == 128) ? launch_gemm_bn<128>(ta, tb, out, ws, M, N, p, err, stream)
-                                  : launch_gemm_bn<64>(ta, tb, out, ws, M, N, p, err, stream);
+  // Half-width B tiles for a split last wave (the same map when unused).
+  CUtensorMap tb_half = tb;
+  if (p.total_units > p.full_units && !make_tmap_bf16(&tb_half, w, N, K, p.bn / 2))
+    return cudaErrorInvalidValue;
+  cudaError_t e =
+      (p.bn == 256)   ? launch_gemm_bn<256>(ta, tb, tb_half, out, ws, M, N, p, err, stream)
+      : (p.bn == 128) ? launch_gemm_bn<128>(ta, tb, tb_half, out, ws, M, N, p, err, stream)
+                      : launch_gemm_bn<64>(ta, tb, tb_half, out, ws, M, N, p, err, stream);
   if (e != cudaSuccess) return e;
   if (p.splits > 1) {
     const int64_t n4 = M * N / 4;
