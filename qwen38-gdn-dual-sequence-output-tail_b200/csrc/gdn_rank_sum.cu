@@ -219,10 +219,12 @@ int32_t gdn_b200_rank_sum(const gdn_b200_tail_group_v1* group, uint32_t epoch, i
     if (q != me) ready.flag[ready.count++] = gdn::flag_ready(group, L, q);
   gdn::rank_flags_wait_kernel<<<1, 32, 0, c>>>(ready, epoch, err);
   if ((st = launch_check("ready wait")) != STATECENTRIC_QWEN38_OK) return st;
-  // 3. ...this rank's rows of it, pulled by the copy engines (rank order)...
+  // 3. ...this rank's rows of it, pulled by the copy engines, starting at
+  // the next rank: at every point of the sequence each rank's memory serves
+  // one puller instead of all of them reading rank 0, then rank 1, ...
   uint8_t* staging = gdn::region(group, me) + L.staging_off + b * W * L.slot_bytes;
-  for (int q = 0; q < W; ++q) {
-    if (q == me) continue;
+  for (int step = 1; step < W; ++step) {
+    const int q = (me + step) % W;
     const uint8_t* src = gdn::region(group, q) + b * L.part_bytes +
                          static_cast<uint64_t>(me) * shard_bytes;
     const cudaError_t e = cudaMemcpyAsync(staging + q * L.slot_bytes, src, shard_bytes,
