@@ -182,6 +182,16 @@ def workload_desc(nseq: int) -> str:
             f"Hk={QK_HEADS} Hv={V_HEADS} D=128 hidden={HIDDEN}, chunk 64")
 
 
+def resolve_reduce(reduce: str, gpus: int) -> str:
+    """The rank-sum method for --reduce on `gpus` GPUs.  Measured on 8 B200s
+    (bench workload): the copy-engine reduce-scatter wins up to 4 GPUs
+    (N = 2: 0.430 ms against 0.520 ms with NCCL's reduce-scatter), NCCL's
+    reduce-scatter at 8 (0.729 against 0.796 ms)."""
+    if reduce != "auto":
+        return reduce
+    return "ce" if gpus <= 4 else "rs"
+
+
 def use_fused_reduce(world: int, reduce: str) -> bool:
     return world > 1 and reduce == "fused"
 
@@ -530,11 +540,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
-    if args.reduce == "auto":
-        # Measured on 8 B200s (bench workload): the copy-engine reduce-scatter
-        # wins up to 4 GPUs (N = 2: 0.430 ms against 0.520 ms with NCCL's
-        # reduce-scatter), NCCL's reduce-scatter at 8 (0.729 against 0.796 ms).
-        args.reduce = "ce" if args.gpus <= 4 else "rs"
+    args.reduce = resolve_reduce(args.reduce, args.gpus)
     if args.impl == "reference":
         run_reference(args)
         return
