@@ -139,12 +139,15 @@ int32_t gdn_b200_output_tail(const void* o, const void* z, const void* gamma, co
   const int K = value_heads * GDN_B200_HEAD_DIM;
   uint16_t* gated = reinterpret_cast<uint16_t*>(ws + kErrBytes);
   float* gemm_ws = reinterpret_cast<float*>(ws + kErrBytes + round256(static_cast<uint64_t>(rows) * K * 2));
-  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
-  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync");
-  if (rows == 0) return ok();
+  cudaError_t e;
+  if (rows == 0) {
+    e = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
+    return e == cudaSuccess ? ok() : cuda_status(e, "cudaMemsetAsync");
+  }
+  // The prologue clears the error word (no separate memset on the stream).
   e = gdn::launch_tail_prologue(static_cast<const uint16_t*>(o), static_cast<const uint16_t*>(z),
                                 static_cast<const uint16_t*>(gamma), gated, rows, value_heads,
-                                eps, s);
+                                eps, s, err);
   if (e != cudaSuccess) return cuda_status(e, "tail prologue launch");
   e = gdn::launch_tail_gemm(gated, static_cast<const uint16_t*>(w_out),
                             static_cast<uint16_t*>(out), gemm_ws, rows, hidden, K, err, s,
@@ -354,12 +357,13 @@ static int32_t chunk_prefill_impl(const gdn::ChunkTable& tab, const void* q, con
                                   const void* v, const void* a, const void* b,
                                   const float* A_log, const float* dt_bias, float* state,
                                   void* o_out, int32_t qk_heads, int32_t value_heads,
-                                  uint8_t* scratch, uint32_t* err, cudaStream_t s) {
+                                  uint8_t* scratch, uint32_t* err, cudaStream_t s,
+                                  bool clear_err = false) {
   cudaError_t e = gdn::launch_chunk_prefill(
       tab, static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
       static_cast<const uint16_t*>(v), static_cast<const uint16_t*>(a),
       static_cast<const uint16_t*>(b), A_log, dt_bias, state, static_cast<uint16_t*>(o_out),
-      qk_heads, value_heads, scratch, err, s);
+      qk_heads, value_heads, scratch, err, s, clear_err);
   return cuda_status(e, "chunk prefill launch");
 }
 
@@ -410,7 +414,7 @@ static int32_t layer_forward_impl(const gdn::ChunkTable& tab, const void* q, con
                                   const float* A_log, const float* dt_bias, const void* gamma,
                                   const void* w_out, float* state, void* out, int32_t qk_heads,
                                   int32_t value_heads, int32_t hidden, uint8_t* ws, uint32_t* err,
-                                  cudaStream_t s) {
+                                  cudaStream_t s, bool clear_err = false) {
   const int64_t T = tab.cu[tab.num_seqs];
   const int64_t K = static_cast<int64_t>(value_heads) * GDN_B200_HEAD_DIM;
   uint64_t off = 0;
@@ -422,7 +426,11 @@ static int32_t layer_forward_impl(const gdn::ChunkTable& tab, const void* q, con
   uint8_t* records = ws + off;
   if (!decode) off += round256(gdn::chunk_workspace_bytes(tab, qk_heads, value_heads));
   float* gemm_ws = reinterpret_cast<float*>(ws + off);
-  if (T == 0) return ok();
+  if (T == 0) {
+    if (!clear_err) return ok();
+    const cudaError_t e0 = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
+    return e0 == cudaSuccess ? ok() : cuda_status(e0, "cudaMemsetAsync");
+  }
   cudaError_t e;
   if (decode) {
     e = gdn::launch_decode(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
@@ -430,11 +438,11 @@ static int32_t layer_forward_impl(const gdn::ChunkTable& tab, const void* q, con
                            static_cast<const uint16_t*>(b), A_log, dt_bias, state, nullptr,
                            static_cast<const uint16_t*>(z), static_cast<const uint16_t*>(gamma),
                            gated, tab.num_seqs, qk_heads, value_heads, s, nullptr, err,
-                           w_out, static_cast<uint64_t>(hidden) * K * 2);
+                           w_out, static_cast<uint64_t>(hidden) * K * 2, clear_err);
     if (e != cudaSuccess) return cuda_status(e, "decode launch");
   } else {
     const int32_t r = chunk_prefill_impl(tab, q, k, v, a, b, A_log, dt_bias, state, o, qk_heads,
-                                         value_heads, records, err, s);
+                                         value_heads, records, err, s, clear_err);
     if (r != STATECENTRIC_QWEN38_OK) return r;
     e = gdn::launch_tail_prologue(o, static_cast<const uint16_t*>(z),
                                   static_cast<const uint16_t*>(gamma), gated, T, value_heads,
@@ -501,10 +509,10 @@ int32_t gdn_b200_layer_forward(const void* q, const void* k, const void* v, cons
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint32_t* err = reinterpret_cast<uint32_t*>(ws);
-  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
-  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync");
+  // The layer's first kernel clears the error word (no separate memset).
   return layer_forward_impl(tab, q, k, v, a, b, z, A_log, dt_bias, gamma, w_out, state, out,
-                            qk_heads, value_heads, hidden, ws + kErrBytes, err, s);
+                            qk_heads, value_heads, hidden, ws + kErrBytes, err, s,
+                            /*clear_err=*/true);
 }
 
 // ------------------------------------------------------- input side ----

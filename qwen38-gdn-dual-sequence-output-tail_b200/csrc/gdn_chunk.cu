@@ -250,7 +250,10 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
                       const uint16_t* __restrict__ b, const float* __restrict__ A_log,
                       const float* __restrict__ dt_bias, uint8_t* __restrict__ kq_records,
                       uint8_t* __restrict__ records, int qk_heads, int value_heads,
-                      uint32_t* err) {
+                      uint32_t* err, int clear_err) {
+  // With clear_err the call's error word starts at zero here instead of by a
+  // separate memset (errors are recorded only after bounded waits of seconds).
+  if (clear_err && blockIdx.x == 0 && threadIdx.x == 0) *err = 0u;
   extern __shared__ uint8_t smem_raw[];
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1141,8 +1144,11 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
                                  const uint16_t* v, const uint16_t* a, const uint16_t* b,
                                  const float* A_log, const float* dt_bias, float* state,
                                  uint16_t* o_out, int qk_heads, int value_heads,
-                                 uint8_t* scratch, uint32_t* err, cudaStream_t stream) {
-  if (tab.total_chunks == 0) return cudaSuccess;
+                                 uint8_t* scratch, uint32_t* err, cudaStream_t stream,
+                                 bool clear_err) {
+  if (tab.total_chunks == 0) {
+    return clear_err ? cudaMemsetAsync(err, 0, sizeof(uint32_t), stream) : cudaSuccess;
+  }
   const int64_t tokens = tab.cu[tab.num_seqs];
   uint8_t* kq_records = scratch;
   uint8_t* records = scratch + static_cast<uint64_t>(tab.total_chunks) * qk_heads * kKQBytes;
@@ -1167,7 +1173,8 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
   const int64_t units = static_cast<int64_t>(tab.total_chunks) * qk_heads;
   const int pgrid = static_cast<int>(std::min<int64_t>(units, 3 * static_cast<int64_t>(sms)));
   gdn_chunk_prep_kernel<<<pgrid, kPrepThreads, prep_smem, stream>>>(
-      tab, tq, tk, a, b, A_log, dt_bias, kq_records, records, qk_heads, value_heads, err);
+      tab, tq, tk, a, b, A_log, dt_bias, kq_records, records, qk_heads, value_heads, err,
+      clear_err ? 1 : 0);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   note_launches();

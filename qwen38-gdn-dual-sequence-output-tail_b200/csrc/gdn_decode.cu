@@ -102,7 +102,12 @@ gdn_decode_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k
                   const uint16_t* __restrict__ gamma, uint16_t* __restrict__ gated_out,
                   const uint64_t* __restrict__ state_rows, int units, int qk_heads,
                   int value_heads, const uint8_t* __restrict__ l2_pre, uint64_t l2_pre_bytes,
-                  uint32_t* err) {
+                  uint32_t* err, int clear_err) {
+  // With clear_err the call's error word starts at zero here instead of by a
+  // separate memset, before the tail GEMM is let in (errors are recorded only
+  // after bounded waits of seconds, or for a misaligned slot-table row, which
+  // this mode never receives).
+  if (clear_err && blockIdx.x == 0 && threadIdx.x == 0) *err = 0u;
   griddep_launch_dependents();   // the tail GEMM may start streaming W now
   extern __shared__ uint8_t smem_raw[];
   DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(
@@ -299,7 +304,7 @@ cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* 
                           const uint16_t* z, const uint16_t* gamma, uint16_t* gated_out,
                           int batch, int qk_heads, int value_heads, cudaStream_t stream,
                           const uint64_t* state_rows, uint32_t* err, const void* l2_prefetch,
-                          uint64_t l2_prefetch_bytes) {
+                          uint64_t l2_prefetch_bytes, bool clear_err) {
   const int units = batch * value_heads;
   if (units <= 0) return cudaSuccess;
   const uint32_t smem = decode_smem_bytes();
@@ -309,7 +314,8 @@ cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* 
   const int grid = units < sm_count() ? units : sm_count();
   gdn_decode_kernel<<<grid, kDecodeThreads, smem, stream>>>(
       q, k, v, a, b, A_log, dt_bias, state, o_out, z, gamma, gated_out, state_rows, units,
-      qk_heads, value_heads, static_cast<const uint8_t*>(l2_prefetch), l2_prefetch_bytes, err);
+      qk_heads, value_heads, static_cast<const uint8_t*>(l2_prefetch), l2_prefetch_bytes, err,
+      clear_err && state_rows == nullptr ? 1 : 0);
   e = cudaGetLastError();
   if (e == cudaSuccess) note_launches();
   return e;

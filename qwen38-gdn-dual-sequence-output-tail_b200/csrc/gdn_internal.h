@@ -33,7 +33,8 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
                                  const uint16_t* v, const uint16_t* a, const uint16_t* b,
                                  const float* A_log, const float* dt_bias, float* state,
                                  uint16_t* o_out, int qk_heads, int value_heads,
-                                 uint8_t* scratch, uint32_t* err, cudaStream_t stream);
+                                 uint8_t* scratch, uint32_t* err, cudaStream_t stream,
+                                 bool clear_err = false);
 
 cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                           const uint16_t* a, const uint16_t* b, const float* A_log,
@@ -41,7 +42,8 @@ cudaError_t launch_decode(const uint16_t* q, const uint16_t* k, const uint16_t* 
                           const uint16_t* z, const uint16_t* gamma, uint16_t* gated_out,
                           int batch, int qk_heads, int value_heads, cudaStream_t stream,
                           const uint64_t* state_rows = nullptr, uint32_t* err = nullptr,
-                          const void* l2_prefetch = nullptr, uint64_t l2_prefetch_bytes = 0);
+                          const void* l2_prefetch = nullptr, uint64_t l2_prefetch_bytes = 0,
+                          bool clear_err = false);
 // l2_prefetch: a buffer (16-byte aligned) the next kernel on the stream reads,
 // brought into L2 by the decode CTAs once their last state block is loading.
 
@@ -51,7 +53,8 @@ int sm_count();
 uint64_t tail_gemm_workspace_bytes(int64_t M, int N, int K);
 cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uint16_t* gamma,
                                  uint16_t* gated, int64_t rows, int value_heads, float eps,
-                                 cudaStream_t stream);
+                                 cudaStream_t stream,
+                                 uint32_t* clear_err = nullptr);
 // overlap_previous: the previous launch on `stream` is one of this
 // library's kernels (tail prologue or decode) that writes `a` but not `w`;
 // for M <= 128 the GEMM then starts while it runs and streams W early.

@@ -41,7 +41,11 @@ template <int kProloguePairs>
 __global__ void __launch_bounds__(256)
 tail_prologue_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ z,
                      const uint16_t* __restrict__ gamma, uint16_t* __restrict__ gated,
-                     int64_t pairs, float eps) {
+                     int64_t pairs, float eps, uint32_t* __restrict__ clear_err) {
+  // The call's error word starts at zero: cleared here, before the GEMM is
+  // let in, instead of by a separate memset (only the GEMM records errors,
+  // after a bounded wait of seconds).
+  if (clear_err != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *clear_err = 0u;
   griddep_launch_dependents();   // the tail GEMM may start streaming W now
   const int64_t first = static_cast<int64_t>(blockIdx.x) * kPrologueStride * kProloguePairs +
                         (threadIdx.x >> 4);
@@ -607,17 +611,17 @@ uint64_t tail_gemm_workspace_bytes(int64_t M, int N, int K) {
 
 cudaError_t launch_tail_prologue(const uint16_t* o, const uint16_t* z, const uint16_t* gamma,
                                  uint16_t* gated, int64_t rows, int value_heads, float eps,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, uint32_t* clear_err) {
   const int64_t pairs = rows * value_heads;
   if (pairs == 0) return cudaSuccess;
   if (pairs >= kPrologueTwoPairs) {
     const int64_t blocks = (pairs + 2 * kPrologueStride - 1) / (2 * kPrologueStride);
     tail_prologue_kernel<2><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(o, z, gamma, gated,
-                                                                             pairs, eps);
+                                                                             pairs, eps, clear_err);
   } else {
     const int64_t blocks = (pairs + kPrologueStride - 1) / kPrologueStride;
     tail_prologue_kernel<1><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(o, z, gamma, gated,
-                                                                             pairs, eps);
+                                                                             pairs, eps, clear_err);
   }
   const cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) note_launches();
