@@ -392,10 +392,9 @@ int32_t gdn_b200_chunk_prefill(const void* q, const void* k, const void* v, cons
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint32_t* err = reinterpret_cast<uint32_t*>(ws);
-  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(uint32_t), s);
-  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync");
+  // The prep kernel clears the error word (no separate memset).
   return chunk_prefill_impl(tab, q, k, v, a, b, A_log, dt_bias, state, o_out, qk_heads,
-                            value_heads, ws + kErrBytes, err, s);
+                            value_heads, ws + kErrBytes, err, s, /*clear_err=*/true);
 }
 
 // ------------------------------------------------------------ layer ----
