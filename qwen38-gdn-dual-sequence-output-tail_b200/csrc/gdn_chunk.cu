@@ -254,6 +254,9 @@ gdn_chunk_prep_kernel(const __grid_constant__ ChunkTable tab,
   // With clear_err the call's error word starts at zero here instead of by a
   // separate memset (errors are recorded only after bounded waits of seconds).
   if (clear_err && blockIdx.x == 0 && threadIdx.x == 0) *err = 0u;
+  // A state pass launched to overlap this kernel may start its set-up now
+  // (it waits for this grid before it reads a record).
+  griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -681,6 +684,7 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
   const int lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
   const int seq_t0 = tab.cu[seq];
+  griddep_launch_dependents();   // the tail prologue may launch (it waits for this grid)
   const int seq_len = tab.cu[seq + 1] - seq_t0;
   const int nchunks = (seq_len + kChunk - 1) / kChunk;
   const int chunk0 = tab.chunk_start[seq];
@@ -817,6 +821,9 @@ gdn_chunk_state_kernel(const __grid_constant__ ChunkTable tab,
       };
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_o);
+      // Launched to overlap the prep kernel: its records are complete and
+      // visible after this (a no-op for an ordinary launch).
+      griddep_wait();
       int issued = 0;
       for (; issued < 2 && issued < nchunks; ++issued) load_stage(issued);
       if (nchunks > 2) prefetch_stage(2);
@@ -1186,9 +1193,22 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
   dim3 sgrid(kHeadDim / kDvHalf, value_heads, tab.num_seqs);
   CUtensorMap to;
   if (!make_tmap_thd(&to, o_out, tokens, value_heads)) return cudaErrorInvalidValue;
-  gdn_chunk_state_kernel<<<sgrid, kStateThreads, st_smem, stream>>>(
-      tab, tv, to, kq_records, records, state, o_out, qk_heads, value_heads, err);
-  e = cudaGetLastError();
+  // When the prep grid leaves SMs idle (short inputs), the state pass is
+  // launched to overlap it: its CTAs allocate TMEM and load their initial
+  // state there, and wait for the prep grid only before the first record.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = sgrid;
+  cfg.blockDim = dim3(kStateThreads, 1, 1);
+  cfg.dynamicSmemBytes = st_smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pgrid < sms ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, gdn_chunk_state_kernel, tab, tv, to, kq_records, records, state,
+                         o_out, qk_heads, value_heads, err);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e == cudaSuccess) note_launches();
   return e;
 }
