@@ -1193,9 +1193,10 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
   dim3 sgrid(kHeadDim / kDvHalf, value_heads, tab.num_seqs);
   CUtensorMap to;
   if (!make_tmap_thd(&to, o_out, tokens, value_heads)) return cudaErrorInvalidValue;
-  // When the prep grid leaves SMs idle (short inputs), the state pass is
-  // launched to overlap it: its CTAs allocate TMEM and load their initial
-  // state there, and wait for the prep grid only before the first record.
+  // The state pass is launched to overlap the prep kernel: its CTAs take
+  // SMs as prep CTAs leave (at once on the SMs a short input leaves idle),
+  // allocate TMEM, load their initial state and wait for the prep grid only
+  // before the first record (2 x 4096 chunk core 0.255 -> 0.252 ms).
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = sgrid;
   cfg.blockDim = dim3(kStateThreads, 1, 1);
@@ -1205,7 +1206,7 @@ cudaError_t launch_chunk_prefill(const ChunkTable& tab, const uint16_t* q, const
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pgrid < sms ? 1 : 0;
+  cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, gdn_chunk_state_kernel, tab, tv, to, kq_records, records, state,
                          o_out, qk_heads, value_heads, err);
   if (e == cudaSuccess) e = cudaGetLastError();
