@@ -5,7 +5,8 @@
 // -> 64x64 merge (AOT) -> W,U (AOT) -> ChunkGatedDeltaRuleFwdH -> ChunkFwdO
 // with eight permutes and seventeen allocations, and longer prompts fall back
 // to 8-token recurrent slices (run_sequence, P:3387-3469).  Here every chunk
-// of every sequence is processed in two launches.
+// of every sequence is processed in two launches (the second launched to
+// overlap the first's last CTAs).
 //
 // 1. gdn_chunk_prep_kernel: chunk-parallel and persistent (three CTAs per SM,
 //    units of one chunk x one q/k head, the next unit's q/k tile on its way
@@ -14,7 +15,8 @@
 //      [K;Q] K^T on tcgen05 (K K^T and Q K^T in one M=128 MMA),
 //      per v-head: gating g, beta, in-chunk cumsum G (warp scans),
 //      A = beta_i (K K^T)_ij exp(G_i - G_j) (strictly lower),
-//      T = (I + A)^-1 by 16x16 forward substitution and block merges in f32,
+//      T = (I + A)^-1 in f32: 16x16 diagonal blocks by forward substitution,
+//      then block doubling 16 -> 32 -> 64,
 //      P = (Q K^T)_ij exp(G_i - G_j) (j <= i),
 //    stored as 128-byte-swizzled operand images the second kernel feeds
 //    straight to tcgen05: T as a bf16 hi/lo pair (about 16 mantissa bits),
