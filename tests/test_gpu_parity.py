@@ -49,8 +49,12 @@ def oracle_core(x, cu):
 
 # ------------------------------------------------------------------ tail --
 
+# 2400 rows: 19 x 8 tiles of 128 x 256 on 148 SMs leave a last wave of 4
+# tiles, which run as 8 half-width tiles, one of them in the partial last
+# row tile.
 @pytest.mark.parametrize("rows,hv,hidden", [(128, 32, 2048), (1, 32, 2048), (64, 32, 2048),
                                             (130, 32, 2048), (1000, 32, 2048),
+                                            (2400, 32, 2048),
                                             (256, 4, 2048), (96, 8, 384),
                                             (64, 4, 2048), (32, 2, 2048)])
 def test_output_tail_matches_oracle(cuda, rows, hv, hidden):
