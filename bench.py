@@ -10,11 +10,15 @@ evenly across ranks (head-parallel; rank r holds v-heads [r*32/N, (r+1)*32/N)
 and the matching q/k heads and out_proj columns) and every rank processes 2*N
 sequences of 4096 tokens, so the per-rank kernel work is that of one GPU
 ("weak" scaling); the rank-partial [tokens, 2048] outputs are summed inside
-the timed region: on 2 GPUs inside the tail GEMM kernel itself over NVLink
-peer memory, from 4 GPUs by the unfused tail and a bf16 NCCL all-reduce (the
-faster of the two on each, measured; ``--reduce fused|nccl`` forces one).  The end-to-end figure goes through the
-provider ABI, whose output is the rank-partial as in the reference, followed
-by an NCCL all-reduce.  One JSON line is printed by rank 0.
+the timed region as a reduce-scatter that overlaps the next step: over the
+copy engines (peer copies, ``gdn_b200_rank_sum``) up to 4 GPUs and by NCCL's
+reduce-scatter on a communication stream at 8, the faster of the two at each
+N, measured (``--reduce ce|rs|nccl|fused`` forces one).  The end-to-end
+figure goes through the provider ABI, whose output is the rank-partial as in
+the reference, followed by the same reduction; each rank reads back only its
+row shard.  ``--config cfg4`` prints the fixed-work head-parallel line
+instead (16 x 16384 prefill then a 256-sequence decode step per call).  One
+JSON line is printed by rank 0.
 
 ``--impl reference`` times the CPU restatement of the reference path (the
 oracle; the reference itself runs only on Ascend NPUs) on the host cores with
